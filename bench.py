@@ -1,0 +1,635 @@
+"""Benchmark of the kernscope-tune hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl kernscope|reference] [--no-families]
+
+Metric: "bf16 TFLOP/s & HBM GB/s per kernel family as % of
+B200 roofline, 1/2/4/8 GPU".  The headline workload is configuration C2,
+row softmax of 4096 x 8192 bf16 (HBM GB/s of algorithmic bytes: 2 B read +
+2 B written per element); the JSON line also carries, under "families", the
+same measurement for every other family at its benchmark configuration.
+
+A step is one launch of the family's kernel over one batch, through the C ABI
+(``ks_<family>_launch``).  ``value`` is whole-job throughput with inputs
+resident in HBM; ``e2e`` is the same metric through the same C ABI with the
+inputs copied from pinned host memory and the outputs copied back inside the
+timed region.  Multi-GPU (torchrun) is weak scaling: every rank runs one full
+batch of the configuration on its own GPU (rows / M-panels / heads /
+elements of a G-times larger job); the reduction adds its one cross-GPU
+combine (an NCCL all-reduce of the fp64 partial).  Time = max over ranks of
+CUDA-event time, barrier + synchronize on both sides.
+
+Inputs are synthetic (seeded torch RNG on the device) with the
+configurations' shapes and distributions.  Between timed steps the input
+buffers rotate through enough copies that the working set is >= 4x the L2,
+so no step reads its inputs from L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def _traffic_table():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            return json.load(fh)
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# Workloads: per-rank shapes of the benchmark configurations
+# ---------------------------------------------------------------------------
+WORKLOADS = {
+    "softmax": {"config": "C2", "shape": (4096, 8192), "bound": "hbm", "dtype": "bf16",
+                "desc": "row softmax 4096x8192 bf16, x~N(0,2^2)"},
+    "layernorm": {"config": "C3a", "shape": (16384, 4096), "bound": "hbm", "dtype": "bf16",
+                  "desc": "layernorm 16384x4096 bf16, gamma~N(1,0.1), beta~N(0,0.1), eps 1e-5"},
+    "bias_gelu": {"config": "C3b", "shape": (16384, 16384), "bound": "hbm", "dtype": "bf16",
+                  "desc": "bias_gelu (tanh) 16384x16384 bf16, bias[16384]"},
+    "reduction": {"config": "C3c", "shape": (1 << 28,), "bound": "hbm", "dtype": "f32",
+                  "desc": "full fp32 sum of 2^28 uniform[0,1) (fp64 partials, NCCL combine for N>1)"},
+    "matmul": {"config": "C4", "shape": (8192, 8192, 8192), "bound": "tensor", "dtype": "bf16",
+               "desc": "GEMM 8192^3 bf16, fp32 accumulate, A,B~N(0,1/sqrt(K))"},
+    "matmul_65536": {"config": "C4", "shape": (65536, 8192, 8192), "bound": "tensor", "dtype": "bf16",
+                     "desc": "GEMM 65536x8192x8192 bf16"},
+    "flash_attention": {"config": "C5", "shape": (8, 32, 8192, 128), "bound": "tensor", "dtype": "bf16",
+                        "desc": "flash attention fwd causal B8 H32 N8192 d128 bf16"},
+}
+
+
+class Workload:
+    """Device buffers + launch closure for one family at one per-rank shape."""
+
+    def __init__(self, name, shape, rank, world, seed_base=0):
+        import torch
+
+        from kernscope_b200 import native as N
+        from kernscope_b200 import ops
+
+        self.name, self.shape, self.N, self.ops = name, shape, N, ops
+        self.torch = torch
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 * rank + seed_base + 17)
+        self.gen, self.dev = g, dev
+        self.extra = {}
+        if name == "softmax":
+            r, c = shape
+            self.in_bytes, self.out_bytes = r * c * 2, r * c * 2
+            self.alg_bytes, self.flops = r * c * 4, 0
+            self.make = lambda: [(torch.randn((r, c), generator=g, device=dev) * 2.0).to(torch.bfloat16)]
+            self.outs = lambda: [torch.empty((r, c), dtype=torch.bfloat16, device=dev)]
+            self.cfg = ops.default_softmax_config(c)
+        elif name == "layernorm":
+            r, c = shape
+            self.in_bytes, self.out_bytes = r * c * 2 + 2 * c * 2, r * c * 2
+            self.alg_bytes, self.flops = r * c * 4 + 2 * c * 2, 0
+            gamma = (1.0 + 0.1 * torch.randn(c, generator=g, device=dev)).to(torch.bfloat16)
+            beta = (0.1 * torch.randn(c, generator=g, device=dev)).to(torch.bfloat16)
+            self.make = lambda: [torch.randn((r, c), generator=g, device=dev).to(torch.bfloat16), gamma, beta]
+            self.outs = lambda: [torch.empty((r, c), dtype=torch.bfloat16, device=dev)]
+            self.cfg = ops.default_layernorm_config(c)
+        elif name == "bias_gelu":
+            r, c = shape
+            self.in_bytes, self.out_bytes = r * c * 2 + c * 2, r * c * 2
+            self.alg_bytes, self.flops = r * c * 4 + c * 2, 0
+            bias = (0.1 * torch.randn(c, generator=g, device=dev)).to(torch.bfloat16)
+            self.make = lambda: [torch.randn((r, c), generator=g, device=dev).to(torch.bfloat16), bias]
+            self.outs = lambda: [torch.empty((r, c), dtype=torch.bfloat16, device=dev)]
+            self.cfg = ops.default_bias_gelu_config(c, "tanh")
+            self.extra["reference_model_bytes"] = r * c * 2 * 3
+        elif name == "reduction":
+            (n,) = shape
+            self.in_bytes, self.out_bytes = n * 4, 4
+            self.alg_bytes, self.flops = n * 4 + 4, 0
+            self.make = lambda: [torch.rand(n, generator=g, device=dev)]
+            self.outs = lambda: [torch.empty(1, dtype=torch.float32, device=dev),
+                                 torch.empty(1, dtype=torch.float64, device=dev)]
+            self.cfg = ops.default_reduction_config(n, -1)
+        elif name.startswith("matmul"):
+            m, n, k = shape
+            self.in_bytes, self.out_bytes = (m * k + k * n) * 2, m * n * 2
+            self.alg_bytes, self.flops = (m * k + k * n + m * n) * 2, 2 * m * n * k
+            sig = 1.0 / math.sqrt(k)
+            bmat = (torch.randn((k, n), generator=g, device=dev) * sig).to(torch.bfloat16)
+            self.make = lambda: [(torch.randn((m, k), generator=g, device=dev) * sig).to(torch.bfloat16), bmat]
+            self.outs = lambda: [torch.empty((m, n), dtype=torch.bfloat16, device=dev)]
+            self.cfg = ops.default_matmul_config(m, n, k)
+        elif name == "flash_attention":
+            b, h, s, d = shape
+            self.in_bytes, self.out_bytes = 3 * b * h * s * d * 2, b * h * s * d * 2
+            self.alg_bytes = 4 * b * h * s * d * 2
+            self.flops = 4 * d * b * h * s * (s + 1) // 2  # causal count
+            self.make = lambda: [torch.randn((b, h, s, d), generator=g, device=dev).to(torch.bfloat16)
+                                 for _ in range(3)]
+            self.outs = lambda: [torch.empty((b, h, s, d), dtype=torch.bfloat16, device=dev)]
+            self.cfg = ops.default_flash_attention_config(True)
+        else:
+            raise KeyError(name)
+        footprint = self.in_bytes + self.out_bytes
+        self.rotate = 1 if footprint >= 4 * L2_BYTES else int(math.ceil(4 * L2_BYTES / footprint))
+        self.sets = [(self.make(), self.outs()) for _ in range(self.rotate)]
+        self.ws = None
+        if name == "reduction":
+            self.ws = ops.reduction_workspace(self.sets[0][0][0], axis=-1, cfg=self.cfg)
+
+    def launch(self, i, stream=None):
+        ins, outs = self.sets[i % self.rotate]
+        ops = self.ops
+        if self.name == "softmax":
+            ops.softmax(ins[0], out=outs[0], cfg=self.cfg, stream=stream)
+        elif self.name == "layernorm":
+            ops.layernorm(ins[0], ins[1], ins[2], out=outs[0], cfg=self.cfg, stream=stream)
+        elif self.name == "bias_gelu":
+            ops.bias_gelu(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
+        elif self.name == "reduction":
+            ops.reduction(ins[0], axis=-1, out=outs[0], cfg=self.cfg, workspace=self.ws, partial_f64=outs[1],
+                          stream=stream)
+        elif self.name.startswith("matmul"):
+            ops.matmul(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
+        else:
+            ops.flash_attention(ins[0], ins[1], ins[2], causal=True, out=outs[0], cfg=self.cfg, stream=stream)
+
+    def config_name(self):
+        return self.N.kernel_symbol("flash_attention" if self.name == "flash_attention" else
+                                    "matmul" if self.name.startswith("matmul") else self.name, self.cfg)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(nm)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def _dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def _barrier(world):
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(v, world):
+    import torch
+
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _combine(w, world):
+    """The reduction's cross-GPU combine: all-reduce of the fp64 partial."""
+    if world > 1 and w.name == "reduction":
+        import torch.distributed as dist
+
+        dist.all_reduce(w.sets[0][1][1])
+
+
+def measure_device(w, steps, warmup, world, graph=True):
+    """Timed region: `steps` launches on rotating buffers, CUDA events on the
+    launching stream.  Launch loops are captured in a CUDA graph (one graph
+    of `rotate` launches replayed) so host overhead never paces the GPU."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        w.launch(i)
+        _combine(w, world)
+    torch.cuda.synchronize()
+    g = None
+    per_graph = w.rotate if w.rotate > 1 else 1
+    if graph and world == 1:
+        reps = max(1, 8 // per_graph) if per_graph < 8 else 1
+        per_graph *= reps
+        s = torch.cuda.Stream()
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            w.launch(0)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(per_graph):
+                w.launch(i)
+        g.replay()
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    e0.record(stream)
+    if g is not None:
+        full, rem = divmod(steps, per_graph)
+        for _ in range(full):
+            g.replay()
+        for i in range(rem):
+            w.launch(i)
+    else:
+        for i in range(steps):
+            w.launch(i)
+            _combine(w, world)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    _barrier(world)
+    if g is not None:
+        del g
+    return _max_over_ranks(ms, world)
+
+
+def measure_e2e(w, steps, world):
+    """Same metric through the C ABI with host buffers: per step, H2D of the
+    step's inputs from pinned memory, the launch, D2H of the output."""
+    import torch
+
+    from kernscope_b200 import native as N
+
+    ins, outs = w.sets[0]
+    host_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
+    for h, t in zip(host_in, ins):
+        h.copy_(t)
+    host_out = torch.empty(outs[0].shape, dtype=outs[0].dtype, pin_memory=True)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    h2d = sum(t.numel() * t.element_size() for t in ins)
+    d2h = outs[0].numel() * outs[0].element_size()
+
+    def step():
+        for h, t in zip(host_in, ins):
+            N.check("h2d", N.lib.ks_gpu_memcpy_htod(C.c_void_p(t.data_ptr()), C.c_void_p(h.data_ptr()),
+                                                  t.numel() * t.element_size(), sp))
+        w.launch(0)
+        _combine(w, world)
+        N.check("d2h", N.lib.ks_gpu_memcpy_dtoh(C.c_void_p(host_out.data_ptr()), C.c_void_p(outs[0].data_ptr()),
+                                              d2h, sp))
+
+    step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    _barrier(world)
+    return ms, h2d, d2h
+
+
+def _units(w, bound):
+    return (w.flops / 1e12, "TFLOP/s") if bound == "tensor" else (w.alg_bytes / 1e9, "GB/s")
+
+
+def cpu_baseline(name, shape, budget_s=10.0):
+    """The CPU oracle (numpy port of the reference's refs.py) on one core, on
+    a bounded sample of the workload; returns the metric in its unit."""
+    import numpy as np
+
+    from oracle import inputs as oin
+    from oracle import refs as orf
+
+    t_total, units, sample = 0.0, 0.0, ""
+    rows = 1
+    while t_total < budget_s:
+        if name == "softmax":
+            r, c = shape
+            x = oin.baseline_inputs("softmax", shape, seed=1, row0=0, nrows=min(rows, r))["x"]
+            t0 = time.perf_counter(); orf.softmax(x); dt = time.perf_counter() - t0
+            u = x.shape[0] * c * 4 / 1e9; sample = f"{x.shape[0]} of {r} rows"
+        elif name == "layernorm":
+            r, c = shape
+            d = oin.baseline_inputs("layernorm", shape, seed=2, row0=0, nrows=min(rows, r))
+            t0 = time.perf_counter(); orf.layernorm(d["x"], d["gamma"], d["beta"]); dt = time.perf_counter() - t0
+            u = d["x"].shape[0] * c * 4 / 1e9; sample = f"{d['x'].shape[0]} of {r} rows"
+        elif name == "bias_gelu":
+            r, c = shape
+            d = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=0, nrows=min(rows, r))
+            t0 = time.perf_counter(); orf.bias_gelu_tanh(d["x"], d["bias"]); dt = time.perf_counter() - t0
+            u = d["x"].shape[0] * c * 4 / 1e9; sample = f"{d['x'].shape[0]} of {r} rows"
+        elif name == "reduction":
+            (n,) = shape
+            cnt = min(rows * 65536, n)
+            x = oin.baseline_inputs("reduction_full", shape, seed=2, row0=0, nrows=cnt)["x"]
+            t0 = time.perf_counter(); orf.sum_full_f64(x); dt = time.perf_counter() - t0
+            u = cnt * 4 / 1e9; sample = f"{cnt} of {n} elements"
+        elif name.startswith("matmul"):
+            m, n, k = shape
+            d = oin.baseline_inputs("matmul", (m, n, k), seed=3, row0=0, nrows=min(rows * 8, m))
+            t0 = time.perf_counter(); orf.matmul(d["a"], d["b"]); dt = time.perf_counter() - t0
+            u = 2 * d["a"].shape[0] * n * k / 1e12; sample = f"{d['a'].shape[0]} of {m} rows (BLAS threads: numpy default)"
+        else:
+            b, h, s, dd = shape
+            nq = min(rows * 64, s)
+            d = oin.baseline_inputs("attention", (b, h, s, s, dd), seed=4, row0=0, nrows=1)
+            t0 = time.perf_counter(); orf.attention(d["q"][0, s - nq:], d["k"][0], d["v"][0], causal=False)
+            dt = time.perf_counter() - t0
+            # the last nq query rows attend to (almost) every key under the causal mask
+            u = 4 * dd * nq * s / 1e12; sample = f"last {nq} query rows of 1 of {b*h} heads"
+        t_total += dt
+        units += u
+        rows *= 2
+    return units / t_total, sample
+
+
+def run_families(names, args, rank, world):
+    out = {}
+    peaks = _peaks()
+    traffic = _traffic_table()
+    for nm in names:
+        spec = WORKLOADS[nm]
+        try:
+            w = Workload(nm, spec["shape"], rank, world)
+        except Exception as exc:  # noqa: BLE001 - report, keep the other families
+            out[nm] = {"error": str(exc)[:200]}
+            continue
+        try:
+            w.launch(0)
+        except Exception as exc:  # noqa: BLE001
+            out[nm] = {"error": str(exc)[:200]}
+            del w
+            continue
+        steps = max(3, int(args.family_steps))
+        ms = measure_device(w, steps, 3, world)
+        per = ms / steps
+        u, unit = _units(w, spec["bound"])
+        val = u * world / (per / 1e3)
+        peak = peaks["hbm_gbs"] if spec["bound"] == "hbm" else peaks["bf16_tflops"]
+        ach = u / (per / 1e3)
+        out[nm] = {"config": spec["config"], "workload": spec["desc"], "kernel": w.config_name(),
+                   "value": round(val, 2), "unit": unit, "ms_per_step": round(per, 5),
+                   "roofline": {"bound": spec["bound"], "achieved": round(ach, 2), "peak": peak, "unit": unit,
+                                "frac": round(ach / peak, 4), "traffic": traffic.get(nm)}}
+        del w
+        import torch
+
+        torch.cuda.empty_cache()
+    return out
+
+
+def main_reference(args):
+    """--impl reference: the reference's CPU path (the oracle port of
+    refs.py) on the host cores, rank 0 only, bounded samples per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import multiprocessing as mp
+
+    spec = WORKLOADS[args.workload]
+    cores = os.cpu_count() or 1
+    ctx = mp.get_context("spawn")
+    chunk_rows = 64
+    with ctx.Pool(cores) as pool:
+        def one_step():
+            t0 = time.perf_counter()
+            res = pool.map(_ref_chunk, [(args.workload, i * chunk_rows, chunk_rows) for i in range(cores)])
+            return time.perf_counter() - t0, sum(res)
+        for _ in range(args.warmup):
+            one_step()
+        tt, uu = 0.0, 0.0
+        for _ in range(args.steps):
+            dt, u = one_step()
+            tt += dt
+            uu += u
+    val = uu / tt
+    unit = "TFLOP/s" if spec["bound"] == "tensor" else "GB/s"
+    line = {"metric": "bf16 TFLOP/s & HBM GB/s per kernel family as % of B200 roofline",
+            "impl": "reference", "value": round(val, 4), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+            "config": {"workload": spec["desc"], "baseline_config": spec["config"]},
+            "cpu_baseline": {"value": round(val, 4), "unit": unit, "cores": cores, "kind": "port",
+                             "sample": f"{cores} x {chunk_rows}-row chunks per step (numpy restatement of "
+                                       "tests/golden/kernscope_golden/refs.py, one process per core)"},
+            "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def _ref_chunk(job):
+    name, row0, nrows = job
+    from oracle import inputs as oin
+    from oracle import refs as orf
+
+    shape = WORKLOADS[name]["shape"]
+    if name == "softmax":
+        x = oin.baseline_inputs("softmax", shape, seed=1, row0=row0, nrows=nrows)["x"]
+        orf.softmax(x)
+        return x.size * 4 / 1e9
+    if name == "layernorm":
+        d = oin.baseline_inputs("layernorm", shape, seed=2, row0=row0, nrows=nrows)
+        orf.layernorm(d["x"], d["gamma"], d["beta"])
+        return d["x"].size * 4 / 1e9
+    if name == "bias_gelu":
+        d = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=row0, nrows=nrows)
+        orf.bias_gelu_tanh(d["x"], d["bias"])
+        return d["x"].size * 4 / 1e9
+    if name == "reduction":
+        cnt = nrows * 65536
+        x = oin.baseline_inputs("reduction_full", shape, seed=2, row0=row0 * 65536, nrows=cnt)["x"]
+        orf.sum_full_f64(x)
+        return cnt * 4 / 1e9
+    if name.startswith("matmul"):
+        m, n, k = shape
+        d = oin.baseline_inputs("matmul", shape, seed=3, row0=row0, nrows=nrows)
+        orf.matmul(d["a"], d["b"])
+        return 2 * nrows * n * k / 1e12
+    b, h, s, dd = shape
+    d = oin.baseline_inputs("attention", (b, h, s, s, dd), seed=4, row0=0, nrows=1)
+    q = d["q"][0, s - nrows:]
+    orf.attention(q, d["k"][0], d["v"][0])
+    return 4 * dd * q.shape[0] * s / 1e12
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kernscope", choices=("kernscope", "reference"))
+    ap.add_argument("--workload", default="softmax", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-families", action="store_true", help="skip the per-family summary")
+    ap.add_argument("--family-steps", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 200
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return main_reference(args)
+
+    import torch
+
+    rank, world, local = _dist_setup(args)
+    spec = WORKLOADS[args.workload]
+    peaks = _peaks()
+    w = Workload(args.workload, spec["shape"], rank, world)
+    # clocks: sample through a window that contains the timed region
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t_window = time.time()
+    while time.time() - t_window < 0.6:  # ramp the clocks before timing
+        for i in range(16):
+            w.launch(i)
+        torch.cuda.synchronize()
+    ms = measure_device(w, args.steps, args.warmup, world)
+    extra_t = time.time()
+    while time.time() - extra_t < 0.3:
+        for i in range(16):
+            w.launch(i)
+        torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    per = ms / args.steps
+    u, unit = _units(w, spec["bound"])
+    value = u * world / (per / 1e3)
+    achieved = u / (per / 1e3)
+    peak = peaks["hbm_gbs"] if spec["bound"] == "hbm" else peaks["bf16_tflops"]
+    traffic = _traffic_table().get(args.workload)
+    e2e_ms, h2d, d2h = measure_e2e(w, args.e2e_steps, world)
+    e2e_val = u * world / (e2e_ms / args.e2e_steps / 1e3)
+    kernel = w.config_name()
+    del w
+    torch.cuda.empty_cache()
+    fams = None
+    if not args.no_families:
+        names = [n for n in WORKLOADS if n != args.workload]
+        fams = run_families(names, args, rank, world)
+    cpu = None
+    if rank == 0 and world == 1:
+        cv, sample = cpu_baseline(args.workload, spec["shape"], args.cpu_budget)
+        cpu = {"value": round(cv, 4), "unit": unit, "cores": 1, "kind": "port",
+               "sample": sample + " (numpy restatement of tests/golden/kernscope_golden/refs.py, 1 process)"}
+    if rank == 0:
+        line = {
+            "metric": "bf16 TFLOP/s & HBM GB/s per kernel family as % of B200 roofline",
+            "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"],
+            "data": "synthetic (seeded torch RNG on device, configuration distributions)",
+            "config": {"workload": spec["desc"], "baseline_config": spec["config"],
+                       "shape_per_gpu": list(spec["shape"]), "kernel": kernel,
+                       "parallelism": f"dp{world} (weak: one batch per GPU)",
+                       "l2": "rotating input/output sets, working set >= 4x L2 (no step reads inputs from L2)",
+                       "timing": "CUDA events on the launching stream, graph-replayed launch loop, max over ranks"},
+            "roofline": {"bound": spec["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": peaks["source"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if fams is not None:
+            line["families"] = fams
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

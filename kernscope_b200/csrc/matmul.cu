@@ -1,0 +1,399 @@
+// matmul.cu -- C[M,N] = A[M,K] . B[K,N] on the sm_100a tensor cores.
+//
+// The reference family (matmul_gen.cpp:287-402) stages fp32 copies of the
+// tiles in shared memory and accumulates with scalar FMAs.  Here:
+//
+//   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256),
+//     raster grouped by `group_m` M-tiles for L2 reuse;
+//   * warp 0 (one lane) is the TMA producer: per K-block of 64 it loads the
+//     A box [128 rows x 64 K] and BN/64 B boxes [64 K x 64 N], all with the
+//     128-byte swizzle, into a STAGES-deep shared-memory ring (full/empty
+//     mbarriers);
+//   * warp 1 (one lane) issues tcgen05.mma kind::f16 (bf16 x bf16 -> fp32),
+//     M=128, N=BN, K=16, four per K-block, A K-major and B MN-major straight
+//     from the swizzled tiles (no transpose pass), accumulating in TMEM;
+//     tcgen05.commit releases each ring slot and, per tile, signals the
+//     epilogue; warp 1 also owns the TMEM allocation;
+//   * warps 2-5 are the epilogue: each reads its 32-lane quadrant of the
+//     fp32 accumulator with tcgen05.ld, rounds to bf16 once and stores 16-byte
+//     vectors; ACC TMEM buffers let the next tile's MMAs run meanwhile.
+//
+// Every mbarrier wait is bounded (KsWait): on timeout the kernel records the
+// error word, waits (bounded) for its own TMA loads and MMAs, frees TMEM and
+// returns.  No multicast loads anywhere.
+#include <cmath>
+
+#include "ks_common.cuh"
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;                    // one 128-byte swizzle row of bf16
+constexpr int kUmmaK = 16;
+constexpr int kThreads = 192;              // 6 warps: producer, MMA, 4 x epilogue
+constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB per stage
+constexpr uint32_t kBBoxBytes = kBK * 64 * 2;  // one B box: 64 K-rows x 64 N-cols = 8 KB
+
+template <int BN, int STAGES, int ACC>
+struct MmLayout {
+  static constexpr uint32_t b_bytes = kBK * BN * 2;
+  static constexpr uint32_t a_off = 0;
+  static constexpr uint32_t b_off = a_off + STAGES * kABytes;
+  static constexpr uint32_t bar_off = b_off + STAGES * b_bytes;
+  // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
+  static constexpr uint32_t n_bars = 2 * STAGES + 2 * ACC + 1;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
+  static constexpr uint32_t bytes = misc_off + 16;
+  static constexpr uint32_t smem_request = bytes + 1024;  // slack to align the base to 1024
+  static constexpr uint32_t tmem_cols_raw = ACC * BN;
+  static constexpr uint32_t tmem_cols = tmem_cols_raw <= 32 ? 32 : tmem_cols_raw <= 64 ? 64
+                                        : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
+};
+
+KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &tn) {
+  const int group_size = group_m * num_n;
+  const int g = t / group_size;
+  const int first_m = g * group_m;
+  const int gm = min(num_m - first_m, group_m);
+  const int r = t - g * group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int BN, int STAGES, int ACC>
+__global__ void __launch_bounds__(kThreads, 1)
+    matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
+  using L = MmLayout<BN, STAGES, ACC>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ks_smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + ACC;
+  uint64_t *drain = bars + 2 * STAGES + 2 * ACC;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + kBM - 1) / kBM, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ks_mbar_init(full + s, 1);
+      ks_mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < ACC; ++a) {
+      ks_mbar_init(tfull + a, 1);
+      ks_mbar_init(tempty + a, 4);
+    }
+    ks_mbar_init(drain, 1);
+    *abort = 0;
+    ks_fence_mbar_init();
+    ks_prefetch_tmap(&tma_a);
+    ks_prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) {
+    ks_tmem_alloc(tmem_slot, L::tmem_cols);
+    ks_tmem_relinquish();
+  }
+  ks_tc_fence_before();
+  __syncthreads();
+  ks_tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0, armed_parity = 0;  // per-stage bits for the teardown wait
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!ks_mbar_wait(empty + stage, phase ^ 1u, abort, wait)) {
+          ok = false;
+          break;
+        }
+        uint8_t *a_dst = smem + L::a_off + stage * kABytes;
+        uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
+        ks_mbar_arrive_expect_tx(full + stage, kABytes + L::b_bytes);
+        ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j)
+          ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // teardown: every load this thread issued must have landed before exit
+    for (int s = 0; s < STAGES; ++s)
+      if (armed & (1u << s)) ks_mbar_wait(full + s, (armed_parity >> s) & 1u, nullptr, wait);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = ks_idesc_bf16_f32(kBM, BN, false, true);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int i = 0;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
+      const int acc = i % ACC;
+      const uint32_t acc_phase = (i / ACC) & 1;
+      if (!ks_mbar_wait(tempty + acc, acc_phase ^ 1u, abort, wait)) break;
+      ks_tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!ks_mbar_wait(full + stage, phase, abort, wait)) {
+          ok = false;
+          break;
+        }
+        ks_tc_fence_after();
+        const uint32_t a_addr = ks_smem_u32(smem + L::a_off + stage * kABytes);
+        const uint32_t b_addr = ks_smem_u32(smem + L::b_off + stage * L::b_bytes);
+#pragma unroll
+        for (int k = 0; k < kBK / kUmmaK; ++k) {
+          // A: K-major, 128-byte rows, 8-row groups 1024 bytes apart; step 32 bytes per K=16.
+          const uint64_t adesc = ks_umma_desc_sw128(a_addr + k * 32, 16, 1024);
+          // B: MN-major, 64-column boxes kBBoxBytes apart (LBO), 8 K-rows 1024 bytes apart (SBO);
+          // step 16 K-rows = 2048 bytes per K=16.
+          const uint64_t bdesc = ks_umma_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
+          ks_umma_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
+        }
+        ks_umma_commit(empty + stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) ks_umma_commit(tfull + acc);
+    }
+    // teardown: all MMAs issued by this thread complete before TMEM is freed
+    ks_umma_commit(drain);
+    ks_mbar_wait(drain, 0, nullptr, wait);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+      const int acc = i % ACC;
+      const uint32_t acc_phase = (i / ACC) & 1;
+      if (!ks_mbar_wait(tfull + acc, acc_phase, abort, wait)) break;
+      ks_tc_fence_after();
+      int tm, tn;
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      const int64_t row = int64_t(tm) * kBM + row_in_tile;
+      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        ks_tmem_ld32(t_addr + cc * 32, r);
+        ks_tmem_wait_ld();
+        const int col0 = tn * BN + cc * 32;
+        if (row < M && num_kb > 0) {
+          uint16_t *dst = c + row * N + col0;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (col0 + v * 8 < N) {
+              uint4 w;
+              w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+              w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+              w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+              w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+              *reinterpret_cast<uint4 *>(dst + v * 8) = w;
+            }
+          }
+        }
+      }
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(tempty + acc);
+    }
+  }
+
+  ks_tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ks_tc_fence_after();
+    ks_tmem_dealloc(tmem_base, L::tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path for shapes the TMA path cannot take (K or N not a multiple
+// of 8, or operands not 16-byte aligned): 64x64 output tile per CTA,
+// 16 x 16 threads with a 4 x 4 register fragment, fp32 accumulate.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) matmul_simt_kernel(const uint16_t *__restrict__ a,
+                                                          const uint16_t *__restrict__ b,
+                                                          uint16_t *__restrict__ c, int M, int N, int K) {
+  __shared__ float as[16][64 + 1];
+  __shared__ float bs[16][64 + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int mm = i / 16, kk = i % 16;
+      const int gm = m0 + mm, gk = k0 + kk;
+      as[kk][mm] = (gm < M && gk < K) ? ks_bf16_to_f32(a[int64_t(gm) * K + gk]) : 0.f;
+      const int kb = i / 64, nn = i % 64;
+      const int gn = n0 + nn, gkb = k0 + kb;
+      bs[kb][nn] = (gn < N && gkb < K) ? ks_bf16_to_f32(b[int64_t(gkb) * N + gn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        av[u] = as[kk][ty + 16 * u];
+        bv[u] = bs[kk][tx + 16 * u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int gm = m0 + ty + 16 * u, gn = n0 + tx + 16 * v;
+      if (gm < M && gn < N) c[int64_t(gm) * N + gn] = ks_f32_to_bf16(acc[u][v]);
+    }
+}
+
+bool tc_shape_ok(const ks_matmul_args &a) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return a.k % 8 == 0 && a.n % 8 == 0 && al(a.a) && al(a.b) && al(a.out) && a.m < (1LL << 31) &&
+         a.n < (1LL << 31) && a.k < (1LL << 31);
+}
+
+template <int BN, int STAGES, int ACC>
+int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
+  using L = MmLayout<BN, STAGES, ACC>;
+  CUtensorMap ta, tb;
+  int s = ks::encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, uint64_t(a.k), uint64_t(a.m),
+                             uint64_t(a.k) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != KS_OK) return s;
+  s = ks::encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, uint64_t(a.n), uint64_t(a.k),
+                         uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != KS_OK) return s;
+  auto kern = matmul_tc_kernel<BN, STAGES, ACC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  const int64_t tiles = ((a.m + kBM - 1) / kBM) * ((a.n + BN - 1) / BN);
+  const int sms = ks::sm_count();
+  const int grid = int(tiles < sms ? tiles : sms);
+  kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n),
+                                                int(a.k), cfg.group_m, ks::wait_ctx());
+  return ks::map_cuda(cudaGetLastError());
+}
+
+// Stage counts instantiated per tile width (the ring must fit 227 KB).
+template <int BN>
+constexpr int max_stages() { return BN == 256 ? 4 : 6; }
+
+template <int BN, int ACC>
+int launch_tc_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
+  switch (cfg.stages) {
+    case 2: return launch_tc<BN, 2, ACC>(cfg, a, st);
+    case 3: return launch_tc<BN, 3, ACC>(cfg, a, st);
+    case 4: return launch_tc<BN, 4, ACC>(cfg, a, st);
+    case 5: if constexpr (max_stages<BN>() >= 5) return launch_tc<BN, 5, ACC>(cfg, a, st);
+      return KS_ERR_INVALID_CONFIG;
+    case 6: if constexpr (max_stages<BN>() >= 6) return launch_tc<BN, 6, ACC>(cfg, a, st);
+      return KS_ERR_INVALID_CONFIG;
+    default: return KS_ERR_INVALID_CONFIG;
+  }
+}
+
+constexpr uint32_t kSmemLimit = 227 * 1024;
+
+uint32_t smem_for(int bn, int stages) {
+  return uint32_t(stages) * (kABytes + uint32_t(kBK) * bn * 2) + (2 * stages + 5) * 8 + 16 + 1024;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_t k, char *reason, size_t len) {
+  if (!cfg) return KS_ERR_INVALID_ARGS;
+  if (cfg->tile_m != 128) {
+    ks::set_reason(reason, len, "matmul: tile_m must be 128 (one UMMA M=128 accumulator per CTA)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256) {
+    ks::set_reason(reason, len, "matmul: tile_n must be 64, 128 or 256 (sm_100a space)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->tile_k != 64) {
+    ks::set_reason(reason, len, "matmul: tile_k must be 64 (one 128-byte swizzle row of bf16)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->stages < 2 || cfg->stages > (cfg->tile_n == 256 ? 4 : 6)) {
+    ks::set_reason(reason, len, "matmul: stages must be 2..%d for tile_n %d", cfg->tile_n == 256 ? 4 : 6,
+                   cfg->tile_n);
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->acc_stages != 1 && cfg->acc_stages != 2) {
+    ks::set_reason(reason, len, "matmul: acc_stages must be 1 or 2 (TMEM accumulator buffers)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->group_m < 1 || cfg->group_m > 64) {
+    ks::set_reason(reason, len, "matmul: group_m must be 1..64");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  const uint32_t smem = smem_for(cfg->tile_n, cfg->stages);
+  if (smem > kSmemLimit) {
+    ks::set_reason(reason, len, "matmul: %u bytes of shared memory for %d stages of 128x%dx64 > %u", smem,
+                   cfg->stages, cfg->tile_n, kSmemLimit);
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (m < 0 || n < 0 || k < 0) {
+    ks::set_reason(reason, len, "matmul: negative shape");
+    return KS_ERR_INVALID_ARGS;
+  }
+  ks::set_reason(reason, len, "");
+  return KS_OK;
+}
+
+int ks_matmul_launch(const ks_matmul_config *cfg, const ks_matmul_args *a, void *stream) {
+  if (!cfg || !a) return KS_ERR_INVALID_ARGS;
+  int s = ks_matmul_validate(cfg, a->m, a->n, a->k, nullptr, 0);
+  if (s != KS_OK) return s;
+  if (a->m == 0 || a->n == 0) return KS_OK;
+  if (!a->a || !a->b || !a->out) return KS_ERR_INVALID_ARGS;
+  if ((s = ks::check_arch_sm100()) != KS_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->k == 0)  // empty inner dimension: C = 0
+    return ks::map_cuda(cudaMemsetAsync(a->out, 0, size_t(a->m) * size_t(a->n) * 2, st));
+  if (!tc_shape_ok(*a)) {
+    if (a->m >= (1LL << 31) || a->n >= (1LL << 31) || a->k >= (1LL << 31)) return KS_ERR_INVALID_ARGS;
+    dim3 grid(unsigned((a->n + 63) / 64), unsigned((a->m + 63) / 64));
+    matmul_simt_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t *>(a->a), static_cast<const uint16_t *>(a->b),
+                                             static_cast<uint16_t *>(a->out), int(a->m), int(a->n), int(a->k));
+    return ks::map_cuda(cudaGetLastError());
+  }
+  const bool two = cfg->acc_stages == 2;
+  switch (cfg->tile_n) {
+    case 64: return two ? launch_tc_stages<64, 2>(*cfg, *a, st) : launch_tc_stages<64, 1>(*cfg, *a, st);
+    case 128: return two ? launch_tc_stages<128, 2>(*cfg, *a, st) : launch_tc_stages<128, 1>(*cfg, *a, st);
+    default: return two ? launch_tc_stages<256, 2>(*cfg, *a, st) : launch_tc_stages<256, 1>(*cfg, *a, st);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,185 @@
+"""Torch-tensor front end of the C ABI (device memory and streams from torch).
+
+Each function validates dtype/layout, builds the family's config and args
+structs, and calls ``ks_<family>_launch`` on the current torch stream.  Any
+non-zero status raises ``KsError``; there is no CPU or library fallback.
+
+Default configurations are the sm_100a picks for the benchmark shapes; the
+tuner (``kernscope-tune``) searches the full config spaces.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import native as N
+
+
+def _stream_ptr(stream=None) -> C.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _check_bf16_2d(name, t):
+    if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+        raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+
+
+def _pow2_block(cols: int, vec: int, per_thread: int) -> int:
+    want = max(1, cols // (vec * per_thread))
+    b = 128
+    while b < want and b < 1024:
+        b *= 2
+    return b
+
+
+def default_softmax_config(cols: int) -> N.SoftmaxConfig:
+    vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
+    block = _pow2_block(cols, vec, 4)
+    mode = N.KS_MODE_ONEPASS if cols <= block * 32 else N.KS_MODE_TWOPASS
+    return N.SoftmaxConfig(block, vec, mode)
+
+
+def default_layernorm_config(cols: int) -> N.LayerNormConfig:
+    vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
+    block = _pow2_block(cols, vec, 4)
+    mode = N.KS_MODE_ONEPASS if cols <= block * 32 else N.KS_MODE_TWOPASS
+    return N.LayerNormConfig(block, vec, mode)
+
+
+def default_bias_gelu_config(cols: int, gelu: str = "tanh") -> N.BiasGeluConfig:
+    vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
+    return N.BiasGeluConfig(256, vec, N.KS_GELU_TANH if gelu == "tanh" else N.KS_GELU_ERF)
+
+
+def default_reduction_config(cols: int, axis: int) -> N.ReductionConfig:
+    if axis == -1:
+        return N.ReductionConfig(512, 4, N.KS_MODE_STRIDED)
+    vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
+    return N.ReductionConfig(256, vec, N.KS_MODE_TREE)
+
+
+def default_matmul_config(m: int, n: int, k: int) -> N.MatmulConfig:
+    if n >= 256 and m * n >= 2048 * 2048:
+        return N.MatmulConfig(128, 256, 64, 4, 2, 8)
+    return N.MatmulConfig(128, 128, 64, 6, 2, 8)
+
+
+def default_flash_attention_config(causal: bool) -> N.FlashAttentionConfig:
+    return N.FlashAttentionConfig(128, 128, 2, 1 if causal else 0)
+
+
+def softmax(x: torch.Tensor, out=None, cfg=None, stream=None) -> torch.Tensor:
+    _check_bf16_2d("x", x)
+    rows, cols = x.shape
+    out = torch.empty_like(x) if out is None else out
+    cfg = cfg or default_softmax_config(cols)
+    args = N.SoftmaxArgs(x.data_ptr(), out.data_ptr(), rows, cols)
+    N.check("ks_softmax_launch", N.lib.ks_softmax_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def layernorm(x, gamma, beta, eps: float = 1e-5, out=None, cfg=None, stream=None) -> torch.Tensor:
+    for nm, t in (("x", x), ("gamma", gamma), ("beta", beta)):
+        _check_bf16_2d(nm, t)
+    rows, cols = x.shape
+    out = torch.empty_like(x) if out is None else out
+    cfg = cfg or default_layernorm_config(cols)
+    args = N.LayerNormArgs(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), rows, cols, eps)
+    N.check("ks_layernorm_launch", N.lib.ks_layernorm_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def bias_gelu(x, bias, gelu: str = "tanh", out=None, cfg=None, stream=None) -> torch.Tensor:
+    _check_bf16_2d("x", x)
+    _check_bf16_2d("bias", bias)
+    cols = bias.numel()
+    out = torch.empty_like(x) if out is None else out
+    cfg = cfg or default_bias_gelu_config(cols, gelu)
+    args = N.BiasGeluArgs(x.data_ptr(), bias.data_ptr(), out.data_ptr(), x.numel(), cols)
+    N.check("ks_bias_gelu_launch", N.lib.ks_bias_gelu_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+_DT = {torch.bfloat16: N.KS_BF16, torch.float32: N.KS_F32}
+
+
+def reduction_args(x, out, axis: int, out_dtype, workspace=None, partial_f64=None) -> N.ReductionArgs:
+    rows, cols = (x.shape[0], x.numel() // x.shape[0]) if x.dim() >= 1 else (1, 1)
+    if x.dim() == 1:
+        rows, cols = 1, x.numel()
+    return N.ReductionArgs(x.data_ptr(), out.data_ptr(), rows, cols, _DT[x.dtype], _DT[out_dtype], axis,
+                           workspace.data_ptr() if workspace is not None else None,
+                           workspace.numel() if workspace is not None else 0,
+                           partial_f64.data_ptr() if partial_f64 is not None else None)
+
+
+def reduction_workspace(x, axis: int = 0, out_dtype=None, cfg=None) -> torch.Tensor:
+    out_dtype = out_dtype or x.dtype
+    cols = x.numel() // x.shape[0] if x.dim() > 1 else x.numel()
+    cfg = cfg or default_reduction_config(cols, axis)
+    dummy = torch.empty(1, dtype=out_dtype, device=x.device)
+    args = reduction_args(x, dummy, axis, out_dtype)
+    n = C.c_size_t(0)
+    N.check("ks_reduction_workspace_bytes",
+            N.lib.ks_reduction_workspace_bytes(C.byref(cfg), C.byref(args), C.byref(n)))
+    return torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=x.device)
+
+
+def reduction(x, axis: int = 0, out_dtype=None, out=None, cfg=None, workspace=None, partial_f64=None,
+              stream=None) -> torch.Tensor:
+    """axis 0: y[j] = sum_i x[i, j]; axis -1: full sum of x (fp32 in/out)."""
+    if not (x.is_cuda and x.is_contiguous() and x.dtype in _DT):
+        raise ValueError("x must be a contiguous bf16/fp32 CUDA tensor")
+    out_dtype = out_dtype or x.dtype
+    cols = x.numel() // x.shape[0] if x.dim() > 1 else x.numel()
+    if out is None:
+        out = torch.empty(1 if axis == -1 else cols, dtype=out_dtype, device=x.device)
+    cfg = cfg or default_reduction_config(cols, axis)
+    if workspace is None:
+        workspace = reduction_workspace(x, axis, out_dtype, cfg)
+    args = reduction_args(x, out, axis, out_dtype, workspace, partial_f64)
+    N.check("ks_reduction_launch", N.lib.ks_reduction_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def matmul(a, b, out=None, cfg=None, stream=None) -> torch.Tensor:
+    _check_bf16_2d("a", a)
+    _check_bf16_2d("b", b)
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError("inner dimensions differ")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device) if out is None else out
+    cfg = cfg or default_matmul_config(m, n, k)
+    args = N.MatmulArgs(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k)
+    N.check("ks_matmul_launch", N.lib.ks_matmul_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def flash_attention(q, k, v, causal: bool = True, scale: float = 0.0, out=None, cfg=None,
+                    stream=None) -> torch.Tensor:
+    """q [B,H,Nq,d], k/v [B,H,Nk,d] (or [Nq,d]/[Nk,d] single head)."""
+    for nm, t in (("q", q), ("k", k), ("v", v)):
+        _check_bf16_2d(nm, t)
+    if q.dim() == 2:
+        b, h, nq, d = 1, 1, q.shape[0], q.shape[1]
+        nk = k.shape[0]
+    else:
+        b, h, nq, d = q.shape
+        nk = k.shape[2]
+    out = torch.empty_like(q) if out is None else out
+    cfg = cfg or default_flash_attention_config(causal)
+    cfg.causal = 1 if causal else 0
+    args = N.FlashAttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, h, nq, nk, d, scale)
+    N.check("ks_flash_attention_launch",
+            N.lib.ks_flash_attention_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def device_error_take() -> int:
+    w = C.c_int(0)
+    N.check("ks_device_error_take", N.lib.ks_device_error_take(C.byref(w)))
+    return w.value

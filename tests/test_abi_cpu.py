@@ -1,0 +1,83 @@
+"""CPU: the C-ABI library loads, exports every symbol the header declares, and
+rejects invalid configs/args without touching a GPU."""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kernscope_b200.h")
+
+
+@pytest.fixture(scope="module")
+def N():
+    from kernscope_b200 import native
+
+    return native
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ks_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_symbols_exported(N):
+    names = _declared()
+    assert len(names) >= 40
+    for n in names:
+        assert hasattr(N.lib, n), f"{n} declared in the header but not exported"
+    assert set(names) == set(N.PROTOTYPES), set(names) ^ set(N.PROTOTYPES)
+
+
+def test_abi_version_and_status(N):
+    assert N.lib.ks_abi_version() == 1
+    assert N.status_string(0) == "ok"
+    assert N.status_string(N.KS_ERR_INVALID_CONFIG) == "invalid_config"
+    assert N.status_string(-5) == "launch_failed"  # GpuError::kLaunchFailed
+
+
+def test_validate_rowops(N):
+    assert N.validate("softmax", N.SoftmaxConfig(256, 8, 0), 4096, 8192) == (0, "")
+    st, reason = N.validate("softmax", N.SoftmaxConfig(128, 8, 0), 4096, 8192)
+    assert st == N.KS_ERR_INVALID_CONFIG and "registers" in reason
+    assert N.validate("softmax", N.SoftmaxConfig(128, 8, 1), 4096, 8192)[0] == 0
+    assert N.validate("layernorm", N.LayerNormConfig(512, 8, 0), 16384, 4096)[0] == 0
+    assert N.validate("layernorm", N.LayerNormConfig(512, 3, 0), 16384, 4096)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("bias_gelu", N.BiasGeluConfig(256, 8, 1), 1 << 28, 16384)[0] == 0
+    assert N.validate("bias_gelu", N.BiasGeluConfig(256, 8, 2), 64, 16)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("softmax", N.SoftmaxConfig(256, 8, 0), 0, 64)[0] == N.KS_ERR_INVALID_ARGS
+
+
+def test_validate_matmul(N):
+    assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 8), 8192, 8192, 8192)[0] == 0
+    st, reason = N.validate("matmul", N.MatmulConfig(128, 256, 64, 5, 2, 8), 64, 64, 64)
+    assert st == N.KS_ERR_INVALID_CONFIG and "stages" in reason
+
+
+def test_reduction_workspace_sizes(N):
+    cfg = N.ReductionConfig(512, 4, N.KS_MODE_STRIDED)
+    args = N.ReductionArgs(None, None, 1, 1 << 28, N.KS_F32, N.KS_F32, -1, None, 0, None)
+    n = C.c_size_t(0)
+    assert N.lib.ks_reduction_workspace_bytes(C.byref(cfg), C.byref(args), C.byref(n)) == 0
+    assert 256 < n.value < 1 << 20
+    args.in_dtype = N.KS_BF16
+    assert N.lib.ks_reduction_workspace_bytes(C.byref(cfg), C.byref(args), C.byref(n)) == N.KS_ERR_INVALID_CONFIG
+
+
+def test_kernel_symbols(N):
+    assert N.kernel_symbol("softmax", N.SoftmaxConfig(256, 8, 0)) == "kernscope_b200_softmax_b256_v8_onepass"
+    assert N.kernel_symbol("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 8)) == \
+        "kernscope_b200_matmul_m128_n256_k64_s4_a2_g8"
+    assert N.kernel_symbol("flash_attention", N.FlashAttentionConfig(128, 128, 2, 1)).endswith("_causal")
+
+
+def test_launch_without_gpu_reports_error(N):
+    """Launch calls with null pointers fail with invalid_args before any CUDA call."""
+    cfg = N.SoftmaxConfig(256, 8, 0)
+    args = N.SoftmaxArgs(None, None, 4, 64)
+    assert N.lib.ks_softmax_launch(C.byref(cfg), C.byref(args), None) == N.KS_ERR_INVALID_ARGS
