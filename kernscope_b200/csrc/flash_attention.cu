@@ -1,20 +1,482 @@
-// flash_attention.cu -- causal / non-causal attention forward for sm_100a.
+// flash_attention.cu -- attention forward (causal or not) on the sm_100a
+// tensor cores.
+//
+// The reference family (flash_attention_gen.cpp:255-404) is a scalar
+// FlashAttention-lite: per Br-row query tile it walks Bc-row K/V tiles with
+// the online softmax (m, l, O rescale), S in shared memory, scalar dot
+// products.  Same algorithm here (Dao et al. 2022, online softmax), mapped to
+// Blackwell:
+//
+//   * one CTA = one (batch*head, 256-query block) = two 128-row Q tiles;
+//     K/V walked in 128-row tiles through a 2-stage TMA ring;
+//   * warp 8 (one lane): TMA producer (Q once, K_j and V_j per tile,
+//     128-byte swizzle, 3-D maps [BH][N][d] so out-of-range rows read zeros);
+//   * warp 9 (one lane): tcgen05.mma issuer.  TMEM columns: S0 [0,128),
+//     S1 [128,256), O0 [256,384), O1 [384,512) (fp32, lane = query row).
+//     Issue order per K/V tile j: PV0(j-1), S0(j), PV1(j-1), S1(j) -- each
+//     S MMA reuses the TMEM of the P its own tile just consumed (tcgen05
+//     MMAs of one thread execute in issue order), and each softmax warpgroup
+//     works while the tensor core runs the other tile's MMAs;
+//   * warps 0-3 / 4-7: softmax warpgroups for Q tile 0 / 1.  Thread t owns
+//     query row t: tcgen05.ld of its 128 scores, scale by log2(e)/sqrt(d),
+//     causal / length mask, running max m and sum l in registers (no
+//     shuffles), P = exp2(s - m) rounded to bf16 and written back into TMEM
+//     (columns [0,64) of its S region, two bf16 per column) as the A operand
+//     of O += P V.  O is rescaled only when the running max grows by more
+//     than 2^8 (values exp2(s - m) stay <= 256, exact in fp32/bf16 range);
+//     the final O / l is rounded to bf16 once and stored;
+//   * heavy (late) query blocks launch first for causal load balance.
+//
+// All waits are bounded (KsWait); teardown waits for outstanding TMA loads
+// and MMAs before TMEM is freed.
+#include <cmath>
+
 #include "ks_common.cuh"
+
+namespace {
+
+constexpr int kTile = 128;               // query rows per tile, K/V rows per tile
+constexpr int kD = 128;                  // head dim
+constexpr int kThreads = 320;            // 8 softmax warps + producer + MMA
+constexpr uint32_t kBox = 128 * 64 * 2;  // [128 rows x 64 cols] bf16 box = 16 KB
+constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
+constexpr int kStages = 2;
+
+struct FaLayout {
+  static constexpr uint32_t q_off = 0;                           // Q0, Q1
+  static constexpr uint32_t k_off = q_off + 2 * kTileBytes;      // K[stages]
+  static constexpr uint32_t v_off = k_off + kStages * kTileBytes;  // V[stages]
+  static constexpr uint32_t bar_off = v_off + kStages * kTileBytes;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full, drain
+  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 1 + 1;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
+  static constexpr uint32_t bytes = misc_off + 16;
+  static constexpr uint32_t smem_request = bytes + 1024;
+};
+
+KS_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+KS_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// S(tile g) = Q_g K_j^T: M=128, N=128 (keys), K=d=128 in 8 steps of 16.
+// Q and K tiles are K-major: two 64-column boxes of 128 rows (16 KB apart),
+// 128-byte rows, 8-row groups 1024 bytes apart.
+KS_DEV void issue_s(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, false);
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+    ks_umma_ss(d_tmem, ks_umma_desc_sw128(q_addr + off, 16, 1024), ks_umma_desc_sw128(k_addr + off, 16, 1024),
+               idesc, kk > 0);
+  }
+}
+
+// O(tile g) (+)= P_g V_j: M=128, N=d=128, K=128 keys in 8 steps of 16.
+// P comes from TMEM (8 columns = 16 bf16 per step); V is MN-major: two
+// 64-column boxes 16 KB apart (LBO), 8 key-rows 1024 bytes apart (SBO),
+// 16 key-rows = 2048 bytes per step.
+KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, true);
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk)
+    ks_umma_ts(o_tmem, p_tmem + kk * 8, ks_umma_desc_sw128(v_addr + kk * 2048, kBox, 1024), idesc,
+               accumulate || kk > 0);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
+                  float scale_log2, int causal, KsWait wait) {
+  using L = FaLayout;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ks_smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off);
+  uint64_t *q_full = bars;
+  uint64_t *k_full = bars + 1;
+  uint64_t *v_full = bars + 1 + kStages;
+  uint64_t *kv_empty = bars + 1 + 2 * kStages;
+  uint64_t *s_full = bars + 1 + 3 * kStages;
+  uint64_t *p_full = s_full + 2;
+  uint64_t *o_full = p_full + 2;
+  uint64_t *drain = o_full + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qb = (nq + 2 * kTile - 1) / (2 * kTile);
+  const int qb = num_qb - 1 - int(blockIdx.x);  // heaviest causal blocks first
+  const int bh = blockIdx.y;
+  const int q0 = qb * 2 * kTile;
+  // number of K/V tiles this block needs
+  int n_kv = (nk + kTile - 1) / kTile;
+  if (causal) {
+    const int q_last = min(q0 + 2 * kTile, nq) - 1;
+    n_kv = min(n_kv, q_last / kTile + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    ks_mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      ks_mbar_init(k_full + s, 1);
+      ks_mbar_init(v_full + s, 1);
+      ks_mbar_init(kv_empty + s, 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      ks_mbar_init(s_full + g, 1);
+      ks_mbar_init(p_full + g, 4);
+    }
+    ks_mbar_init(o_full, 1);
+    ks_mbar_init(drain, 1);
+    *abort = 0;
+    ks_fence_mbar_init();
+    ks_prefetch_tmap(&tm_q);
+    ks_prefetch_tmap(&tm_k);
+    ks_prefetch_tmap(&tm_v);
+  }
+  if (warp == 9) {
+    ks_tmem_alloc(tmem_slot, 512);
+    ks_tmem_relinquish();
+  }
+  ks_tc_fence_before();
+  __syncthreads();
+  ks_tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint8_t *qs = smem + L::q_off;
+      ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      for (int g = 0; g < 2; ++g)
+        for (int h = 0; h < 2; ++h) ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64,
+                                                   q0 + g * kTile, bh);
+      uint32_t armed = 0, armed_par = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!ks_mbar_wait(kv_empty + st, ph ^ 1u, abort, wait)) break;
+        uint8_t *ks = smem + L::k_off + st * kTileBytes;
+        uint8_t *vs = smem + L::v_off + st * kTileBytes;
+        ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
+        for (int h = 0; h < 2; ++h) ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, bh);
+        ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
+        for (int h = 0; h < 2; ++h) ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, bh);
+        armed |= 1u << st;
+        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+      }
+      // teardown: the loads issued above have landed
+      ks_mbar_wait(q_full, 0, nullptr, wait);
+      for (int s = 0; s < kStages; ++s)
+        if (armed & (1u << s)) {
+          ks_mbar_wait(k_full + s, (armed_par >> s) & 1u, nullptr, wait);
+          ks_mbar_wait(v_full + s, (armed_par >> s) & 1u, nullptr, wait);
+        }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      const uint32_t q_addr = ks_smem_u32(smem + L::q_off);
+      const uint32_t k_addr = ks_smem_u32(smem + L::k_off);
+      const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
+      const uint32_t t_s[2] = {tmem + 0, tmem + 128};
+      const uint32_t t_o[2] = {tmem + 256, tmem + 384};
+      bool ok = ks_mbar_wait(q_full, 0, abort, wait) && ks_mbar_wait(k_full, 0, abort, wait);
+      if (ok) {
+        ks_tc_fence_after();
+        issue_s(t_s[0], q_addr, k_addr);
+        ks_umma_commit(s_full + 0);
+        issue_s(t_s[1], q_addr + kTileBytes, k_addr);
+        ks_umma_commit(s_full + 1);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int st1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        const bool more = j + 1 < n_kv;
+        if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
+        // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
+        if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
+        ks_tc_fence_after();
+        issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
+        if (more) {
+          if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
+          ks_tc_fence_after();
+          issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
+          ks_umma_commit(s_full + 0);
+        }
+        // tile 1
+        if (!ks_mbar_wait(p_full + 1, j & 1, abort, wait)) break;
+        ks_tc_fence_after();
+        issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0);
+        ks_umma_commit(kv_empty + st);
+        if (more) {
+          issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
+          ks_umma_commit(s_full + 1);
+        }
+      }
+      ks_umma_commit(o_full);
+      ks_umma_commit(drain);
+      ks_mbar_wait(drain, 0, nullptr, wait);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int g = warp >> 2;         // Q tile of this warpgroup
+    const int qd = warp & 3;         // TMEM lane quadrant
+    const int row = qd * 32 + lane;  // row within the tile = TMEM lane
+    const int qrow = q0 + g * kTile + row;
+    const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t s_col = g * 128, o_col = 256 + g * 128;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!ks_mbar_wait(s_full + g, j & 1, abort, wait)) {
+        ok = false;
+        break;
+      }
+      ks_tc_fence_after();
+      uint32_t r[128];
+      ks_tmem_ld32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      ks_tmem_ld32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      ks_tmem_ld32(lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      ks_tmem_ld32(lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      ks_tmem_wait_ld();
+      const int kv0 = j * kTile;
+      // keys beyond this row's limit are masked: causal (key > query) and length
+      int lim = nk - kv0;  // number of valid keys in this tile
+      if (causal) lim = min(lim, qrow - kv0 + 1);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float s = __uint_as_float(r[c]) * scale_log2;
+        s = c < lim ? s : -INFINITY;
+        r[c] = __float_as_uint(s);
+        mx = fmaxf(mx, s);
+      }
+      const float m_new = fmaxf(m, mx);
+      const bool grow = m_new > m + 8.f;  // also true on the first finite max
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O has absorbed every earlier P V (the S commit follows it), rescale.
+        const float alpha = grow ? ex2(m - m_new) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+          ks_tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(lane_addr + o_col + c * 32, o);
+        }
+        ks_tmem_wait_st();
+      }
+      if (grow) {
+        l *= ex2(m - m_new);
+        m = m_new;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float rs = 0.f;
+      uint32_t p[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float a = ex2(__uint_as_float(r[2 * c]) - mu);
+        const float b = ex2(__uint_as_float(r[2 * c + 1]) - mu);
+        p[c] = ks_pack_bf16x2(a, b);
+        // the sum uses the bf16-rounded P that the MMA consumes
+        rs += ks_bf16_lo(p[c]) + ks_bf16_hi(p[c]);
+      }
+      l += rs;
+      tmem_st32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&p[0]));
+      tmem_st32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&p[32]));
+      ks_tmem_wait_st();
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(p_full + g);
+    }
+    // epilogue: O / l -> bf16 -> out[bh, qrow, :]
+    if (ok && ks_mbar_wait(o_full, 0, abort, wait)) {
+      ks_tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint16_t *dst = out + (int64_t(bh) * nq + qrow) * kD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+        ks_tmem_wait_ld();
+        if (qrow < nq) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+            w.y = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+            w.z = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+            w.w = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+            *reinterpret_cast<uint4 *>(dst + c * 32 + v * 8) = w;
+          }
+        }
+      }
+    }
+  }
+
+  ks_tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ks_tc_fence_after();
+    ks_tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path for head dims other than 128 (d <= 256; the reference's gate
+// shapes use d = 16 and 32): one warp per query row, keys in chunks of 32
+// (one key per lane for the scores), online softmax with warp shuffles, each
+// lane accumulating d/32 output columns.
+// ---------------------------------------------------------------------------
+constexpr int kSimtMaxD = 256;
+
+__global__ void __launch_bounds__(128) fa_simt_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+                                                      const uint16_t *__restrict__ v, uint16_t *__restrict__ out,
+                                                      int nq, int nk, int d, float scale_log2, int causal) {
+  __shared__ float qs[4][kSimtMaxD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  const int64_t bh = blockIdx.y;
+  if (row >= nq) return;
+  const uint16_t *qr = q + (bh * nq + row) * d;
+  for (int c = lane; c < d; c += 32) qs[warp][c] = ks_bf16_to_f32(qr[c]);
+  __syncwarp();
+  const uint16_t *kb = k + bh * nk * d;
+  const uint16_t *vb = v + bh * nk * d;
+  const int kend = causal ? min(nk, row + 1) : nk;
+  float m = -INFINITY, l = 0.f;
+  float o[kSimtMaxD / 32];
+#pragma unroll
+  for (int i = 0; i < kSimtMaxD / 32; ++i) o[i] = 0.f;
+  for (int k0 = 0; k0 < kend; k0 += 32) {
+    const int key = k0 + lane;
+    float s = -INFINITY;
+    if (key < kend) {
+      const uint16_t *kr = kb + int64_t(key) * d;
+      float acc = 0.f;
+      for (int c = 0; c < d; ++c) acc = fmaf(qs[warp][c], ks_bf16_to_f32(kr[c]), acc);
+      s = acc * scale_log2;
+    }
+    const float mx = ks_warp_max(s);
+    const float m_new = fmaxf(m, mx);
+    const float alpha = ex2(m - m_new);
+    const float p = (key < kend) ? ex2(s - m_new) : 0.f;
+    l = l * alpha + ks_warp_sum(p);
+#pragma unroll
+    for (int i = 0; i < kSimtMaxD / 32; ++i) o[i] *= alpha;
+    const int nkeys = min(32, kend - k0);
+    for (int t = 0; t < nkeys; ++t) {
+      const float pt = __shfl_sync(0xffffffffu, p, t);
+      const uint16_t *vr = vb + int64_t(k0 + t) * d;
+#pragma unroll
+      for (int i = 0; i < kSimtMaxD / 32; ++i) {
+        const int c = lane + 32 * i;
+        if (c < d) o[i] = fmaf(pt, ks_bf16_to_f32(vr[c]), o[i]);
+      }
+    }
+    m = m_new;
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  uint16_t *orow = out + (bh * nq + row) * d;
+#pragma unroll
+  for (int i = 0; i < kSimtMaxD / 32; ++i) {
+    const int c = lane + 32 * i;
+    if (c < d) orow[c] = ks_f32_to_bf16(o[i] * inv);
+  }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
 
 extern "C" {
 
 int ks_flash_attention_validate(const ks_flash_attention_config *cfg, const ks_flash_attention_args *a,
                                 char *reason, size_t len) {
   if (!cfg || !a) return KS_ERR_INVALID_ARGS;
-  ks::set_reason(reason, len, "flash_attention: not built yet");
-  return KS_ERR_UNSUPPORTED;
+  if (cfg->tile_m != 128 || cfg->tile_n != 128) {
+    ks::set_reason(reason, len, "flash_attention: tile_m and tile_n must be 128 (UMMA M=128 tiles, sm_100a space)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->stages != 2) {
+    ks::set_reason(reason, len, "flash_attention: stages must be 2 (K/V ring depth)");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (cfg->causal != 0 && cfg->causal != 1) {
+    ks::set_reason(reason, len, "flash_attention: causal must be 0 or 1");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (a->d < 1 || a->d > kSimtMaxD) {
+    ks::set_reason(reason, len, "flash_attention: head dim %lld unsupported (1..256; tensor cores at d = 128)",
+                   (long long)a->d);
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (a->batch <= 0 || a->heads <= 0 || a->nq <= 0 || a->nk <= 0) {
+    ks::set_reason(reason, len, "flash_attention: batch, heads, nq, nk must be positive");
+    return KS_ERR_INVALID_ARGS;
+  }
+  if (a->batch * a->heads > 65535 || a->nq >= (1LL << 31) || a->nk >= (1LL << 31)) {
+    ks::set_reason(reason, len, "flash_attention: batch*heads <= 65535 and sequence lengths < 2^31");
+    return KS_ERR_INVALID_ARGS;
+  }
+  ks::set_reason(reason, len, "");
+  return KS_OK;
 }
 
 int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_flash_attention_args *a,
                               void *stream) {
-  (void)stream;
-  if (!cfg || !a) return KS_ERR_INVALID_ARGS;
-  return KS_ERR_UNSUPPORTED;
+  int s = ks_flash_attention_validate(cfg, a, nullptr, 0);
+  if (s != KS_OK) return s;
+  if (!a->q || !a->k || !a->v || !a->out) return KS_ERR_INVALID_ARGS;
+  if ((s = ks::check_arch_sm100()) != KS_OK) return s;
+  const uint64_t bh = uint64_t(a->batch * a->heads);
+  const float scale = a->scale > 0.f ? a->scale : 1.f / sqrtf(float(a->d));
+  const float scale_log2 = scale * 1.4426950408889634f;
+  if (a->d != kD || !aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) {
+    dim3 grid(unsigned((a->nq + 3) / 4), unsigned(bh));
+    fa_simt_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t *>(a->q), static_cast<const uint16_t *>(a->k),
+        static_cast<const uint16_t *>(a->v), static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), int(a->d),
+        scale_log2, cfg->causal);
+    return ks::map_cuda(cudaGetLastError());
+  }
+  CUtensorMap tq, tk, tv;
+  const uint64_t rs = kD * 2;
+  s = ks::encode_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->q, kD, uint64_t(a->nq), bh, rs,
+                         rs * uint64_t(a->nq), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s == KS_OK)
+    s = ks::encode_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->k, kD, uint64_t(a->nk), bh, rs,
+                           rs * uint64_t(a->nk), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s == KS_OK)
+    s = ks::encode_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->v, kD, uint64_t(a->nk), bh, rs,
+                           rs * uint64_t(a->nk), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != KS_OK) return s;
+  cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(FaLayout::smem_request));
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  dim3 grid(unsigned((a->nq + 2 * kTile - 1) / (2 * kTile)), unsigned(bh));
+  fa_fwd_kernel<<<grid, kThreads, FaLayout::smem_request, static_cast<cudaStream_t>(stream)>>>(
+      tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), scale_log2, cfg->causal,
+      ks::wait_ctx());
+  return ks::map_cuda(cudaGetLastError());
 }
 
 }  // extern "C"

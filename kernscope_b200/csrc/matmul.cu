@@ -376,11 +376,12 @@ int ks_matmul_launch(const ks_matmul_config *cfg, const ks_matmul_args *a, void 
   int s = ks_matmul_validate(cfg, a->m, a->n, a->k, nullptr, 0);
   if (s != KS_OK) return s;
   if (a->m == 0 || a->n == 0) return KS_OK;
-  if (!a->a || !a->b || !a->out) return KS_ERR_INVALID_ARGS;
+  if (!a->out) return KS_ERR_INVALID_ARGS;
   if ((s = ks::check_arch_sm100()) != KS_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (a->k == 0)  // empty inner dimension: C = 0
+  if (a->k == 0)  // empty inner dimension: C = 0 (A and B may be null)
     return ks::map_cuda(cudaMemsetAsync(a->out, 0, size_t(a->m) * size_t(a->n) * 2, st));
+  if (!a->a || !a->b) return KS_ERR_INVALID_ARGS;
   if (!tc_shape_ok(*a)) {
     if (a->m >= (1LL << 31) || a->n >= (1LL << 31) || a->k >= (1LL << 31)) return KS_ERR_INVALID_ARGS;
     dim3 grid(unsigned((a->n + 63) / 64), unsigned((a->m + 63) / 64));

@@ -115,6 +115,22 @@ def attention(q, k, v, causal: bool = False) -> np.ndarray:
     return to_bf16(np.matmul(p, vf))
 
 
+def attention_abs_weight(q, k, v, causal: bool = False) -> np.ndarray:
+    """rho = softmax(Q K^T / sqrt(d)) |V| in fp32 (single head).
+
+    The scale of the error of any kernel that feeds P to the tensor cores in
+    bf16: |O_kernel - O| <= 2^-9 rho + 2^-9 |O| + fp32 terms, since each
+    p_i carries a relative rounding error <= 2^-9 and |O| <= rho."""
+    qf, kf, vf = to_f32(q), to_f32(k), to_f32(v)
+    s = np.matmul(qf, kf.T) / math.sqrt(qf.shape[-1])
+    if causal:
+        r = np.arange(s.shape[0])[:, None]
+        c = np.arange(s.shape[1])[None, :]
+        s = np.where(c > r, -np.inf, s)
+    e = np.exp(s - np.max(s, axis=-1, keepdims=True))
+    return np.matmul(e / np.sum(e, axis=-1, keepdims=True), np.abs(vf))
+
+
 def attention_bhnd(q, k, v, causal: bool = False, pairs=None) -> np.ndarray:
     """Multi-head attention over [B,H,N,d]: ``attention`` per (b,h).
 

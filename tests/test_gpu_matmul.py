@@ -47,17 +47,33 @@ def test_matmul_golden(ks, path):
     a, b = to_torch(fx["a"]), to_torch(fx["b"])
     for cfg in _configs(N):
         y = to_numpy(ops.matmul(a, b, cfg=cfg))
-        assert_bf16_close(y, fx["expected"])
+        assert_bf16_close(y, fx["expected"], gate=True)
 
 
 def test_matmul_c1_512(ks):
+    """C1 (512^3, the reference profile).  The reference's max_rel_err with
+    eps 1e-6 is ill-conditioned here: its own driver gates matmul at 64^3
+    because a correct fp32-accumulate GEMM drifts past 1e-2 on near-zero
+    outputs at K=512 (tools/tune/src/driver_matmul.cpp:58-66).  So at 512^3
+    the check is the benchmark tolerance (floor rel-err and norm-wise error
+    <= 1e-2) plus the verdict's cosine/pcc thresholds, against the golden and
+    against an fp64 product; every element is also within 2 bf16 ulps of the
+    fp64 product rounded to bf16."""
+    from oracle import metrics as om
+
     N, ops = ks
     inp = oin.generate_inputs("matmul", (512, 512, 512), seed=0)
     exp = orf.matmul(inp["a"], inp["b"])
+    r64 = inp["a"].astype(np.float64) @ inp["b"].astype(np.float64)
     a, b = to_torch(inp["a"]), to_torch(inp["b"])
     for cfg in _configs(N):
         y = to_numpy(ops.matmul(a, b, cfg=cfg))
         assert_bf16_close(y, exp)
+        assert_bf16_close(y, orf.to_bf16(r64))
+        v = om.verdict(y, exp)
+        assert v["cosine"] >= om.COSINE_MIN and v["pcc"] >= om.PCC_MIN, v
+        ulp = np.abs(orf.to_bf16(r64).astype(np.float64)) * 2.0 ** -7 + 2.0 ** -133
+        assert (np.abs(y.astype(np.float64) - r64) <= ulp + 1e-5).all()
 
 
 @pytest.mark.parametrize("shape", [(1, 8, 8), (130, 264, 72), (257, 136, 200), (1000, 520, 1032),
@@ -108,7 +124,7 @@ def test_matmul_8192_sampled(ks):
     ri, ci = rng.integers(0, m, 4096), rng.integers(0, n, 4096)
     got = to_numpy(y[ri.tolist(), ci.tolist()])
     exp = orf.to_bf16(np.einsum("ij,ji->i", af[ri], bf[:, ci]))
-    assert_bf16_close(got, exp, verdict=False)
+    assert_bf16_close(got, exp)
 
 
 def test_matmul_invalid_configs(ks):

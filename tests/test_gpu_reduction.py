@@ -46,7 +46,7 @@ def test_axis0_golden_all_configs(ks, path):
         if c % vec:
             continue
         y = to_numpy(ops.reduction(x, axis=0, cfg=cfg))
-        assert_bf16_close(y, fx["expected"])
+        assert_bf16_close(y, fx["expected"], gate=True)
         ran += 1
     assert ran > 0
 
@@ -58,8 +58,9 @@ def test_axis0_shapes_f32(ks, shape):
     xf = rng.uniform(-1, 1, shape).astype(np.float32)
     y = to_numpy(ops.reduction(to_torch(xf), axis=0, out_dtype=__import__("torch").float32))
     exp = np.sum(xf.astype(np.float64), axis=0)
-    err = np.abs(y.astype(np.float64) - exp) / np.maximum(np.abs(exp), 1e-3 * np.sqrt(shape[0]))
-    assert err.max() < 1e-5 * max(1.0, np.log2(shape[0]))
+    # fp32 summation in any order: |error| <= (n - 1) * 2^-24 * sum |x| (+ output rounding)
+    bound = shape[0] * 2.0 ** -24 * np.sum(np.abs(xf.astype(np.float64)), axis=0) + 2.0 ** -24 * np.abs(exp)
+    assert (np.abs(y.astype(np.float64) - exp) <= bound + 1e-30).all()
 
 
 def test_full_sum_baseline(ks):
