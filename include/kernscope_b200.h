@@ -177,6 +177,23 @@ int ks_reduction_workspace_bytes(const ks_reduction_config *cfg,
 int ks_reduction_launch(const ks_reduction_config *cfg, const ks_reduction_args *args,
                         void *stream);
 
+/* No counterpart in the reference.  ks_reduction_launch for callers that
+ * cannot call cudaMalloc -- e.g. a plugin whose host framework owns all
+ * device memory (its allocator reserved the GPU up front), or a
+ * latency-critical path that cannot take cudaMalloc's device-wide
+ * synchronisation.  Same arguments and results; args->workspace and
+ * args->workspace_bytes are ignored: the partials and counters live in a
+ * library-owned static device array of KS_REDUCTION_NOALLOC_SCRATCH_BYTES,
+ * held on every GPU that loads the library until the process exits.
+ * Returns KS_ERR_WORKSPACE when ks_reduction_workspace_bytes() for these
+ * args exceeds that size.  The first call on each device resolves the
+ * array's device address (do it before any stream capture).  All calls
+ * share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing.                            */
+#define KS_REDUCTION_NOALLOC_SCRATCH_BYTES (1u << 20)
+int ks_reduction_launch_noalloc(const ks_reduction_config *cfg, const ks_reduction_args *args,
+                                void *stream);
+
 /* ---- matmul (matmul_gen.h:97-174) ----------------------------------------
  * C[M,N] = A[M,K] . B[K,N]; A row-major (K contiguous), B row-major
  * (N contiguous), C row-major; bf16 in/out, fp32 accumulate in TMEM.

@@ -13,6 +13,8 @@
 //   partials in the workspace, last CTA sums them in order and writes the
 //   fp32 result (and the fp64 value for a cross-GPU combine).
 // Both are HBM-bound: 4 (fp32) or 2 (bf16) bytes read per element.
+#include <mutex>
+
 #include "ks_common.cuh"
 
 namespace {
@@ -387,3 +389,70 @@ int ks_reduction_launch(const ks_reduction_config *cfg, const ks_reduction_args 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Reduction without caller-provided workspace.
+//
+// Some callers cannot call cudaMalloc: a plugin whose host framework owns all
+// device memory (its allocator reserved the GPU's memory up front, so a
+// direct cudaMalloc fails or competes with it), or a latency-critical path
+// that cannot pay cudaMalloc's device-wide synchronisation.  They still pass
+// their input and output buffers; the per-CTA partials and arrival counters
+// live in the fixed scratch array below instead of a workspace.
+//
+// * The array is kReductionNoallocScratchBytes (1 MiB) and, like any
+//   __device__ variable, is held on every GPU that loads this library until
+//   the process exits.  Launches whose workspace would be larger return
+//   KS_ERR_WORKSPACE.
+// * Host code cannot use the array's name as a device address (it names a
+//   host-side shadow).  The first call on each device resolves the address
+//   with cudaGetSymbolAddress while that device is current and caches it;
+//   make that first call before any stream capture.
+// * Every call shares the one array and it keeps the last call's contents;
+//   the launch clears the arrival counters it needs on the stream before the
+//   kernel.  Calls that overlap on the GPU (concurrent streams, several host
+//   threads) race on the array and must be serialised by the caller.
+// * Nothing here allocates: no cudaMalloc/cudaFree, no allocating library.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kReductionNoallocScratchBytes = size_t(1) << 20;
+static_assert(kReductionNoallocScratchBytes == KS_REDUCTION_NOALLOC_SCRATCH_BYTES, "header and library disagree");
+
+static __device__ __align__(256) unsigned char g_reduction_scratch[kReductionNoallocScratchBytes];
+
+int noalloc_scratch_address(void **out) {
+  constexpr int kMaxDevices = 64;
+  static void *addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  if (dev < 0 || dev >= kMaxDevices) return KS_ERR_DEVICE_NOT_FOUND;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_reduction_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? ks::map_cuda(e) : KS_ERR_OTHER;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return KS_OK;
+}
+
+}  // namespace
+
+extern "C" int ks_reduction_launch_noalloc(const ks_reduction_config *cfg, const ks_reduction_args *args,
+                                           void *stream) {
+  if (!cfg || !args) return KS_ERR_INVALID_ARGS;
+  size_t need = 0;
+  int s = ks_reduction_workspace_bytes(cfg, args, &need);
+  if (s != KS_OK) return s;
+  if (need > kReductionNoallocScratchBytes) return KS_ERR_WORKSPACE;
+  void *scratch = nullptr;
+  if ((s = noalloc_scratch_address(&scratch)) != KS_OK) return s;
+  ks_reduction_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kReductionNoallocScratchBytes;
+  return ks_reduction_launch(cfg, &a, stream);
+}

@@ -139,6 +139,7 @@ PROTOTYPES = {
     "ks_reduction_validate": (C.c_int, [_P(ReductionConfig), _P(ReductionArgs), C.c_char_p, C.c_size_t]),
     "ks_reduction_workspace_bytes": (C.c_int, [_P(ReductionConfig), _P(ReductionArgs), _P(C.c_size_t)]),
     "ks_reduction_launch": (C.c_int, [_P(ReductionConfig), _P(ReductionArgs), C.c_void_p]),
+    "ks_reduction_launch_noalloc": (C.c_int, [_P(ReductionConfig), _P(ReductionArgs), C.c_void_p]),
     "ks_matmul_validate": (C.c_int, [_P(MatmulConfig), C.c_int64, C.c_int64, C.c_int64, C.c_char_p, C.c_size_t]),
     "ks_matmul_launch": (C.c_int, [_P(MatmulConfig), _P(MatmulArgs), C.c_void_p]),
     "ks_flash_attention_validate": (C.c_int, [_P(FlashAttentionConfig), _P(FlashAttentionArgs), C.c_char_p,
