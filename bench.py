@@ -551,6 +551,9 @@ def main():
     ap.add_argument("--family-steps", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--clock-window", type=float, default=0.9,
+                    help="seconds of extra launches around the timed region for the nvidia-smi clock samples "
+                         "(0 when the run is profiled, where every launch is replayed)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200
@@ -569,13 +572,13 @@ def main():
     if sampler:
         sampler.start()
     t_window = time.time()
-    while time.time() - t_window < 0.6:  # ramp the clocks before timing
+    while time.time() - t_window < args.clock_window * 2 / 3:  # ramp the clocks before timing
         for i in range(16):
             w.launch(i)
         torch.cuda.synchronize()
     ms = measure_device(w, args.steps, args.warmup, world)
     extra_t = time.time()
-    while time.time() - extra_t < 0.3:
+    while time.time() - extra_t < args.clock_window / 3:
         for i in range(16):
             w.launch(i)
         torch.cuda.synchronize()

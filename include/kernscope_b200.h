@@ -103,12 +103,15 @@ typedef enum ks_dtype { KS_BF16 = 0, KS_F32 = 1, KS_F64 = 2 } ks_dtype;
  * elem_common.h:49-55).  ONEPASS: the row is read from HBM once and held in
  * registers, both reductions run over registers.  TWOPASS: the row is
  * re-read for the second statistic (second read served by L2), which lifts
- * the register cap on the row length. */
+ * the register cap on the row length.  STAGED (softmax, layernorm): a ring
+ * of whole rows in shared memory filled by bulk copies keeps several rows
+ * per CTA in flight (vec_width 8, cols % 8 == 0, cols <= 16384). */
 typedef enum ks_elem_mode {
   KS_MODE_ONEPASS = 0,
   KS_MODE_TWOPASS = 1,
   KS_MODE_STRIDED = 2,  /* reduction: warp-shuffle combine */
-  KS_MODE_TREE = 3      /* reduction: shared-memory tree combine */
+  KS_MODE_TREE = 3,     /* reduction: shared-memory tree combine */
+  KS_MODE_STAGED = 4
 } ks_elem_mode;
 
 /* ---- softmax (tools/tune/include/kernscope/tune/softmax_gen.h:39-51) ----

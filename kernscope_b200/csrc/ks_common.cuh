@@ -135,6 +135,15 @@ KS_DEV void ks_prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completion counted on `bar` in bytes.
+KS_DEV void ks_bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   ks_smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(ks_smem_u32(bar))
+               : "memory");
+}
+
 KS_DEV void ks_tma_load_2d(void *dst, const CUtensorMap *m, uint64_t *bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"

@@ -146,6 +146,197 @@ KS_DEV void block_reduce_welford(float &n, float &mu, float &m2, float4 *sh) {
 }
 
 // ===========================================================================
+// 8-wide fast paths (vec_width 8, 32-bit in-row indexing).  Written for the
+// fewest instructions per element, since at B200 bandwidth a row op has only
+// ~6-9 issue slots per element before it stops being HBM-bound:
+//   * block max / sum: warp shuffles of plain max / add, one shared slot per
+//     warp, every warp then reduces the <= 32 slots itself.  The two
+//     reductions of a row use different slot arrays, so the next row can
+//     overwrite them without a trailing barrier;
+//   * the row max is taken on the packed words (bf16x2 max, exact);
+//   * exp(x - m) = ex2(x*log2e - m*log2e) as one FFMA + one ex2.
+// ===========================================================================
+KS_DEV float block_max_fast(float v, float *sh) {
+  v = ks_warp_max(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  return ks_warp_max(lane < int(blockDim.x >> 5) ? sh[lane] : -INFINITY);
+}
+KS_DEV float block_sum_fast(float v, float *sh) {
+  v = ks_warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  return ks_warp_sum(lane < int(blockDim.x >> 5) ? sh[lane] : 0.f);
+}
+
+KS_DEV __nv_bfloat162 as_bf162(uint32_t w) { return *reinterpret_cast<__nv_bfloat162 *>(&w); }
+KS_DEV uint32_t as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+KS_DEV float max8_packed(const uint4 &w) {
+  const __nv_bfloat162 a = __hmax2(as_bf162(w.x), as_bf162(w.y));
+  const __nv_bfloat162 b = __hmax2(as_bf162(w.z), as_bf162(w.w));
+  const uint32_t c = as_u32(__hmax2(a, b));
+  return fmaxf(ks_bf16_lo(c), ks_bf16_hi(c));
+}
+KS_DEV void unpack8(const uint4 &w, float (&v)[8]) {
+  v[0] = ks_bf16_lo(w.x); v[1] = ks_bf16_hi(w.x); v[2] = ks_bf16_lo(w.y); v[3] = ks_bf16_hi(w.y);
+  v[4] = ks_bf16_lo(w.z); v[5] = ks_bf16_hi(w.z); v[6] = ks_bf16_lo(w.w); v[7] = ks_bf16_hi(w.w);
+}
+KS_DEV uint4 pack8(const float (&v)[8]) {
+  return make_uint4(ks_pack_bf16x2(v[0], v[1]), ks_pack_bf16x2(v[2], v[3]), ks_pack_bf16x2(v[4], v[5]),
+                    ks_pack_bf16x2(v[6], v[7]));
+}
+
+// Softmax of one row whose chunks (8 bf16 each) this thread holds in w[];
+// chunk k of thread t is row chunk t + k*blockDim.x.  `after_max` runs on
+// thread 0 right after the max reduction's barrier (every thread has then
+// consumed its inputs), used by the staged kernel to refill its ring slot.
+template <int MAXCH, typename AfterMax>
+KS_DEV void softmax_row8(const uint4 (&w)[MAXCH], int nvec, float *sh_max, float *sh_sum, uint4 *yr,
+                         AfterMax after_max) {
+  const int t = threadIdx.x, nt = blockDim.x;
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k)
+    if (t + k * nt < nvec) m = fmaxf(m, max8_packed(w[k]));
+  m = block_max_fast(m, sh_max);
+  after_max();
+  const float mL = m * kLog2e;
+  float e[MAXCH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    if (t + k * nt < nvec) {
+      unpack8(w[k], e[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        e[k][j] = ks_ex2(fmaf(e[k][j], kLog2e, -mL));
+        s += e[k][j];
+      }
+    }
+  }
+  s = block_sum_fast(s, sh_sum);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    if (t + k * nt < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[k][j] *= inv;
+      __stcs(yr + t + k * nt, pack8(e[k]));
+    }
+  }
+}
+
+// Loads this thread's chunks of row r (chunk k = column chunk t + k*blockDim.x).
+template <int MAXCH>
+KS_DEV void load_row8(const uint16_t *__restrict__ x, int r, int cols, int nvec, uint4 (&w)[MAXCH]) {
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + size_t(r) * cols);
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < nvec) w[k] = __ldcs(xr + c);
+  }
+}
+
+// MAXB = largest block the instantiation serves.  Blocks <= 512 threads have
+// the registers to prefetch the next row's packed words while the current
+// row is reduced, which keeps HBM reads in flight through the barriers.
+template <int MAXCH, int MAXB>
+__global__ void __launch_bounds__(MAXB) softmax_onepass_v8_kernel(const uint16_t *__restrict__ x,
+                                                                  uint16_t *__restrict__ y, int rows, int cols) {
+  __shared__ float sh_max[32], sh_sum[32];
+  const int nvec = cols >> 3;
+  constexpr bool kPrefetch = MAXB <= 512;
+  uint4 nxt[MAXCH];
+  if (kPrefetch && int(blockIdx.x) < rows) load_row8<MAXCH>(x, blockIdx.x, cols, nvec, nxt);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    uint4 w[MAXCH];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int k = 0; k < MAXCH; ++k) w[k] = nxt[k];
+      if (r + int(gridDim.x) < rows) load_row8<MAXCH>(x, r + gridDim.x, cols, nvec, nxt);
+    } else {
+      load_row8<MAXCH>(x, r, cols, nvec, w);
+    }
+    softmax_row8<MAXCH>(w, nvec, sh_max, sh_sum, reinterpret_cast<uint4 *>(y + size_t(r) * cols), [] {});
+  }
+}
+
+// Layernorm of one row held as packed chunks: exact two-pass statistics from
+// registers (mean, then the sum of squared deviations), each a plain sum
+// reduction; y = d * (rstd * gamma) + beta with d = x - mean.
+template <int MAXCH, typename AfterFirst>
+KS_DEV void layernorm_row8(const uint4 (&w)[MAXCH], int nvec, float inv_cols, float eps, const uint4 *g4,
+                           const uint4 *b4, float *sh_a, float *sh_b, uint4 *yr, AfterFirst after_first) {
+  const int t = threadIdx.x, nt = blockDim.x;
+  float v[MAXCH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    if (t + k * nt < nvec) {
+      unpack8(w[k], v[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[k][j];
+    }
+  }
+  const float mean = block_sum_fast(s, sh_a) * inv_cols;
+  after_first();
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    if (t + k * nt < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[k][j] -= mean;
+        q = fmaf(v[k][j], v[k][j], q);
+      }
+    }
+  }
+  const float rstd = rsqrtf(block_sum_fast(q, sh_b) * inv_cols + eps);
+#pragma unroll
+  for (int k = 0; k < MAXCH; ++k) {
+    const int c = t + k * nt;
+    if (c < nvec) {
+      float g[8], b[8];
+      unpack8(g4[c], g);
+      unpack8(b4[c], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] = fmaf(v[k][j], rstd * g[j], b[j]);
+      __stcs(yr + c, pack8(v[k]));
+    }
+  }
+}
+
+template <int MAXCH, int MAXB>
+__global__ void __launch_bounds__(MAXB) layernorm_onepass_v8_kernel(const uint16_t *__restrict__ x,
+                                                                    const uint16_t *__restrict__ gamma,
+                                                                    const uint16_t *__restrict__ beta,
+                                                                    uint16_t *__restrict__ y, int rows, int cols,
+                                                                    float inv_cols, float eps) {
+  __shared__ float sh_a[32], sh_b[32];
+  const int nvec = cols >> 3;
+  const uint4 *g4 = reinterpret_cast<const uint4 *>(gamma);
+  const uint4 *b4 = reinterpret_cast<const uint4 *>(beta);
+  constexpr bool kPrefetch = MAXB <= 512;
+  uint4 nxt[MAXCH];
+  if (kPrefetch && int(blockIdx.x) < rows) load_row8<MAXCH>(x, blockIdx.x, cols, nvec, nxt);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    uint4 w[MAXCH];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int k = 0; k < MAXCH; ++k) w[k] = nxt[k];
+      if (r + int(gridDim.x) < rows) load_row8<MAXCH>(x, r + gridDim.x, cols, nvec, nxt);
+    } else {
+      load_row8<MAXCH>(x, r, cols, nvec, w);
+    }
+    layernorm_row8<MAXCH>(w, nvec, inv_cols, eps, g4, b4, sh_a, sh_b,
+                          reinterpret_cast<uint4 *>(y + size_t(r) * cols), [] {});
+  }
+}
+
+// ===========================================================================
 // softmax
 // ===========================================================================
 // ONEPASS: thread t owns vector chunks t, t+B, ..., t+(MAXCH-1)B of the row
@@ -341,13 +532,23 @@ __global__ void __launch_bounds__(1024) layernorm_twopass_kernel(const uint16_t 
 // bias_gelu
 // ===========================================================================
 KS_DEV float gelu_erf(float t) {
-  // 0.5 t (1 + erf(t/sqrt2)) written with erfc to avoid cancellation for t < 0.
-  return 0.5f * t * erfcf(-t * 0.70710678118654752f);
+  // 0.5 t (1 + erf(t/sqrt2)): erf rounded to fp32 before the add, as the
+  // reference does (refs.py:59-63).
+  return 0.5f * t * (1.f + erff(t * 0.70710678118654752f));
 }
 KS_DEV float gelu_tanh(float t) {
   // 0.5 t (1 + tanh(u)) = t * sigmoid(2u), u = sqrt(2/pi) (t + 0.044715 t^3).
   const float u = 0.7978845608028654f * fmaf(0.044715f * t, t * t, t);
   const float e = ks_ex2(-2.f * kLog2e * u);
+  return __fdividef(t, 1.f + e);
+}
+
+// Same function with the constants folded: exp(-2u) = 2^(t * (c1 + c2 t^2)),
+// c1 = -2 log2(e) sqrt(2/pi), c2 = 0.044715 c1; y = t / (1 + 2^(...)).
+constexpr float kGeluC1 = -2.f * 1.4426950408889634f * 0.7978845608028654f;
+constexpr float kGeluC2 = kGeluC1 * 0.044715f;
+KS_DEV float gelu_tanh_fast(float t) {
+  const float e = ks_ex2(t * fmaf(kGeluC2, t * t, kGeluC1));
   return __fdividef(t, 1.f + e);
 }
 
@@ -391,6 +592,49 @@ __global__ void __launch_bounds__(1024) bias_gelu_kernel(const uint16_t *__restr
   }
 }
 
+// 8-wide variant: the loaded words stay packed (4 registers per 8 bf16)
+// until they are used, so UNROLL rows of 16-byte loads are in flight per
+// thread without spilling.
+template <int GELU, int UNROLL>
+__global__ void __launch_bounds__(1024) bias_gelu_v8_kernel(const uint16_t *__restrict__ x,
+                                                            const uint16_t *__restrict__ bias,
+                                                            uint16_t *__restrict__ y, int64_t total, int64_t cols,
+                                                            int64_t rows, int rows_per_cta) {
+  const int64_t nvec = cols / 8;
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= nvec) return;
+  const uint4 bw = __ldg(reinterpret_cast<const uint4 *>(bias) + c);
+  const __nv_bfloat162 bb[4] = {as_bf162(bw.x), as_bf162(bw.y), as_bf162(bw.z), as_bf162(bw.w)};
+  const int64_t r0 = int64_t(blockIdx.y) * rows_per_cta;
+  const int64_t r1 = min(rows, r0 + rows_per_cta);
+  for (int64_t r = r0; r < r1; r += UNROLL) {
+    uint4 w[UNROLL];
+    bool ok[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t off = (r + u) * cols + c * 8;
+      ok[u] = (r + u < r1) && (off + 8 <= total);
+      if (ok[u]) w[u] = __ldcs(reinterpret_cast<const uint4 *>(x + off));
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      if (!ok[u]) continue;
+      const uint32_t in[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+      uint32_t outw[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        // fusion point: bf16 + bf16 added exactly and rounded to bf16 once
+        const uint32_t t2 = as_u32(__hadd2(as_bf162(in[h]), bb[h]));
+        const float t0 = ks_bf16_lo(t2), t1 = ks_bf16_hi(t2);
+        const float g0 = GELU == KS_GELU_TANH ? gelu_tanh_fast(t0) : gelu_erf(t0);
+        const float g1 = GELU == KS_GELU_TANH ? gelu_tanh_fast(t1) : gelu_erf(t1);
+        outw[h] = ks_pack_bf16x2(g0, g1);
+      }
+      __stcs(reinterpret_cast<uint4 *>(y + (r + u) * cols + c * 8), make_uint4(outw[0], outw[1], outw[2], outw[3]));
+    }
+  }
+}
+
 // Scalar tail kernel for a ragged last row whose length is not a multiple
 // of VEC (total % cols != 0 and the tail not VEC-aligned).
 template <int GELU>
@@ -404,10 +648,150 @@ __global__ void bias_gelu_tail_kernel(const uint16_t *__restrict__ x, const uint
   y[i] = ks_f32_to_bf16(GELU == KS_GELU_TANH ? gelu_tanh(t) : gelu_erf(t));
 }
 
+// ===========================================================================
+// STAGED mode (softmax, layernorm): a ring of whole rows in shared memory,
+// each filled by one cp.async.bulk copy.  Thread 0 keeps `stages` rows in
+// flight per CTA and refills a slot as soon as the block reduction of the
+// row in it has completed (its __syncthreads proves every thread has read
+// the slot into registers), so HBM reads never wait on the reductions.
+// Rows need cols % 8 == 0 (16-byte copies); chunks are 8 bf16 wide.
+// ===========================================================================
+constexpr int kMaxStages = 8;
+
+struct RowRing {
+  uint8_t *base;
+  uint32_t stride;  // slot size, rounded up to 128 bytes
+  uint32_t bytes;   // row bytes copied per slot
+  int stages;
+  uint64_t *full;
+};
+
+// Issue the copy of local row `i` (global row blockIdx.x + i*gridDim.x) into slot i % stages.
+KS_DEV void ring_issue(const RowRing &rg, const uint16_t *x, int64_t cols, int64_t i) {
+  const int s = int(i % rg.stages);
+  const int64_t r = blockIdx.x + i * gridDim.x;
+  ks_mbar_arrive_expect_tx(rg.full + s, rg.bytes);
+  ks_bulk_load(rg.base + size_t(s) * rg.stride, x + r * cols, rg.bytes, rg.full + s);
+}
+
+// Teardown after an abort at local row `i`: the copies already issued for
+// rows [i, min(my_rows, i + stages)) must land before the CTA exits.
+KS_DEV void ring_drain(const RowRing &rg, int64_t i, int64_t my_rows, const KsWait &w) {
+  for (int64_t j = i; j < my_rows && j < i + rg.stages; ++j)
+    ks_mbar_wait(rg.full + (j % rg.stages), uint32_t((j / rg.stages) & 1), nullptr, w);
+}
+
+template <int MAXCH>
+__global__ void __launch_bounds__(512) softmax_staged_kernel(const uint16_t *__restrict__ x,
+                                                              uint16_t *__restrict__ y, int64_t rows,
+                                                              int64_t cols, int stages, KsWait wait) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ float sh_max[32], sh_sum[32];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ int abort_flag;
+  const int64_t my_rows = rows > blockIdx.x ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  RowRing rg{dsm, uint32_t((cols * 2 + 127) & ~int64_t(127)), uint32_t(cols * 2), stages, full};
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) ks_mbar_init(full + s, 1);
+    abort_flag = 0;
+    ks_fence_mbar_init();
+    for (int64_t i = 0; i < my_rows && i < stages; ++i) ring_issue(rg, x, cols, i);
+  }
+  __syncthreads();
+  const int nvec = int(cols >> 3);
+  int64_t i = 0;
+  for (; i < my_rows; ++i) {
+    const int s = int(i % stages);
+    if (!ks_mbar_wait(full + s, uint32_t((i / stages) & 1), &abort_flag, wait)) break;
+    const uint4 *row = reinterpret_cast<const uint4 *>(dsm + size_t(s) * rg.stride);
+    uint4 w[MAXCH];
+#pragma unroll
+    for (int k = 0; k < MAXCH; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < nvec) w[k] = row[c];
+    }
+    const int64_t next = i + stages;
+    softmax_row8<MAXCH>(w, nvec, sh_max, sh_sum, reinterpret_cast<uint4 *>(y + (blockIdx.x + i * gridDim.x) * cols),
+                        [&] {
+                          // every thread has read slot s: refill it
+                          if (threadIdx.x == 0 && next < my_rows) {
+                            ks_fence_proxy_async();
+                            ring_issue(rg, x, cols, next);
+                          }
+                        });
+  }
+  if (threadIdx.x == 0 && i < my_rows) ring_drain(rg, i, my_rows, wait);
+}
+
+template <int MAXCH>
+__global__ void __launch_bounds__(512) layernorm_staged_kernel(const uint16_t *__restrict__ x,
+                                                                const uint16_t *__restrict__ gamma,
+                                                                const uint16_t *__restrict__ beta,
+                                                                uint16_t *__restrict__ y, int64_t rows,
+                                                                int64_t cols, float inv_cols, float eps, int stages,
+                                                                KsWait wait) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ float sh_a[32], sh_b[32];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ uint64_t gb_full;
+  __shared__ int abort_flag;
+  const int64_t my_rows = rows > blockIdx.x ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint32_t stride = uint32_t((cols * 2 + 127) & ~int64_t(127));
+  // slots [0, stages) hold rows; then gamma and beta
+  RowRing rg{dsm, stride, uint32_t(cols * 2), stages, full};
+  const uint4 *g_s = reinterpret_cast<const uint4 *>(dsm + size_t(stages) * stride);
+  const uint4 *b_s = reinterpret_cast<const uint4 *>(dsm + size_t(stages + 1) * stride);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) ks_mbar_init(full + s, 1);
+    ks_mbar_init(&gb_full, 1);
+    abort_flag = 0;
+    ks_fence_mbar_init();
+    ks_mbar_arrive_expect_tx(&gb_full, 2 * uint32_t(cols * 2));
+    ks_bulk_load(dsm + size_t(stages) * stride, gamma, uint32_t(cols * 2), &gb_full);
+    ks_bulk_load(dsm + size_t(stages + 1) * stride, beta, uint32_t(cols * 2), &gb_full);
+    for (int64_t i = 0; i < my_rows && i < stages; ++i) ring_issue(rg, x, cols, i);
+  }
+  __syncthreads();
+  const int nvec = int(cols >> 3);
+  const bool gb_ok = ks_mbar_wait(&gb_full, 0, &abort_flag, wait);
+  int64_t i = 0;
+  for (; i < my_rows && gb_ok; ++i) {
+    const int s = int(i % stages);
+    if (!ks_mbar_wait(full + s, uint32_t((i / stages) & 1), &abort_flag, wait)) break;
+    const uint4 *row = reinterpret_cast<const uint4 *>(dsm + size_t(s) * stride);
+    uint4 w[MAXCH];
+#pragma unroll
+    for (int k = 0; k < MAXCH; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < nvec) w[k] = row[c];
+    }
+    const int64_t next = i + stages;
+    layernorm_row8<MAXCH>(w, nvec, inv_cols, eps, g_s, b_s, sh_a, sh_b,
+                          reinterpret_cast<uint4 *>(y + (blockIdx.x + i * gridDim.x) * cols), [&] {
+                            if (threadIdx.x == 0 && next < my_rows) {
+                              ks_fence_proxy_async();
+                              ring_issue(rg, x, cols, next);
+                            }
+                          });
+  }
+  if (threadIdx.x == 0) {
+    if (!gb_ok) ks_mbar_wait(&gb_full, 0, nullptr, wait);
+    if (i < my_rows) ring_drain(rg, i, my_rows, wait);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host-side dispatch helpers
 // ---------------------------------------------------------------------------
 constexpr int kRegElems = 32;  // per-thread register budget for a ONEPASS row
+constexpr uint32_t kStagedRingBytes = 64 * 1024;  // row ring per CTA (3 CTAs fit an SM)
+
+int staged_stages(int64_t cols) {
+  const int64_t stride = (cols * 2 + 127) & ~int64_t(127);
+  int64_t s = kStagedRingBytes / stride;
+  if (s > kMaxStages) s = kMaxStages;
+  return int(s);
+}
 
 bool valid_block(int b) { return b == 128 || b == 256 || b == 512 || b == 1024; }
 bool valid_vec(int v) { return v == 1 || v == 2 || v == 4 || v == 8; }
@@ -415,9 +799,9 @@ bool valid_vec(int v) { return v == 1 || v == 2 || v == 4 || v == 8; }
 bool aligned(const void *p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
 template <typename K>
-int grid_for(K kernel, int block, int64_t work) {
+int grid_for(K kernel, int block, int64_t work, size_t dyn_smem = 0) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, 0) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, dyn_smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   const int64_t cap = int64_t(per_sm) * ks::sm_count();
   return int(work < cap ? work : cap);
@@ -433,8 +817,8 @@ int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, 
     ks::set_reason(reason, len, "%s: vec_width must be 1, 2, 4 or 8 (sm_100a space)", fam);
     return KS_ERR_INVALID_CONFIG;
   }
-  if (mode != KS_MODE_ONEPASS && mode != KS_MODE_TWOPASS) {
-    ks::set_reason(reason, len, "%s: mode must be onepass or twopass", fam);
+  if (mode != KS_MODE_ONEPASS && mode != KS_MODE_TWOPASS && mode != KS_MODE_STAGED) {
+    ks::set_reason(reason, len, "%s: mode must be onepass, twopass or staged", fam);
     return KS_ERR_INVALID_CONFIG;
   }
   if (rows <= 0 || cols <= 0) {
@@ -446,10 +830,17 @@ int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, 
     ks::set_reason(reason, len, "%s: cols %lld not divisible by vec_width %d", fam, (long long)cols, vec);
     return KS_ERR_INVALID_CONFIG;
   }
-  if (mode == KS_MODE_ONEPASS && cols > int64_t(block) * kRegElems) {
+  if ((mode == KS_MODE_ONEPASS || mode == KS_MODE_STAGED) && cols > int64_t(block) * kRegElems) {
     ks::set_reason(reason, len,
-                   "%s: onepass keeps the row in registers: cols %lld > block %d x %d register elements", fam,
-                   (long long)cols, block, kRegElems);
+                   "%s: %s keeps the row in registers: cols %lld > block %d x %d register elements", fam,
+                   mode == KS_MODE_STAGED ? "staged" : "onepass", (long long)cols, block, kRegElems);
+    return KS_ERR_INVALID_CONFIG;
+  }
+  if (mode == KS_MODE_STAGED && (vec != 8 || block > 512 || staged_stages(cols) < 2)) {
+    ks::set_reason(reason, len,
+                   "%s: staged copies whole rows with 16-byte bulk copies: vec_width must be 8, block <= 512 "
+                   "and a two-row ring must fit %u bytes (cols %lld)",
+                   fam, kStagedRingBytes, (long long)cols);
     return KS_ERR_INVALID_CONFIG;
   }
   ks::set_reason(reason, len, "");
@@ -460,9 +851,24 @@ template <int VEC>
 int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, cudaStream_t st) {
   auto x = static_cast<const uint16_t *>(a.x);
   auto y = static_cast<uint16_t *>(a.out);
-  if (cfg.mode == KS_MODE_TWOPASS) {
+  if (cfg.mode == KS_MODE_STAGED) {
+    if constexpr (VEC == 8) {
+      const int stages = staged_stages(a.cols);
+      const size_t shm = size_t(stages) * size_t((a.cols * 2 + 127) & ~int64_t(127));
+      auto k = softmax_staged_kernel<kRegElems / 8>;
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shm));
+      if (e != cudaSuccess) return ks::map_cuda(e);
+      k<<<grid_for(k, cfg.block, a.rows, shm), cfg.block, shm, st>>>(x, y, a.rows, a.cols, stages, ks::wait_ctx());
+    } else {
+      return KS_ERR_INVALID_CONFIG;
+    }
+  } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = softmax_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, y, a.rows, a.cols);
+  } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
+    auto k = cfg.block <= 256 ? softmax_onepass_v8_kernel<kRegElems / 8, 256>
+                              : softmax_onepass_v8_kernel<kRegElems / 8, 1024>;
+    k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, y, int(a.rows), int(a.cols));
   } else {
     constexpr int MAXCH = kRegElems / VEC;
     auto k = softmax_onepass_kernel<VEC, MAXCH>;
@@ -478,9 +884,27 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
   auto b = static_cast<const uint16_t *>(a.beta);
   auto y = static_cast<uint16_t *>(a.out);
   const float eps = a.eps > 0.f ? a.eps : 1e-5f;
-  if (cfg.mode == KS_MODE_TWOPASS) {
+  if (cfg.mode == KS_MODE_STAGED) {
+    if constexpr (VEC == 8) {
+      const int stages = staged_stages(a.cols);
+      const size_t shm = size_t(stages + 2) * size_t((a.cols * 2 + 127) & ~int64_t(127));
+      auto k = layernorm_staged_kernel<kRegElems / 8>;
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shm));
+      if (e != cudaSuccess) return ks::map_cuda(e);
+      k<<<grid_for(k, cfg.block, a.rows, shm), cfg.block, shm, st>>>(x, g, b, y, a.rows, a.cols,
+                                                                     1.f / float(a.cols), eps, stages,
+                                                                     ks::wait_ctx());
+    } else {
+      return KS_ERR_INVALID_CONFIG;
+    }
+  } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = layernorm_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, g, b, y, a.rows, a.cols, eps);
+  } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
+    auto k = cfg.block <= 256 ? layernorm_onepass_v8_kernel<kRegElems / 8, 256>
+                              : layernorm_onepass_v8_kernel<kRegElems / 8, 1024>;
+    k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, g, b, y, int(a.rows), int(a.cols),
+                                                            1.f / float(a.cols), eps);
   } else {
     constexpr int MAXCH = kRegElems / VEC;
     auto k = layernorm_onepass_kernel<VEC, MAXCH>;
@@ -503,7 +927,11 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
   const int64_t rows = (a.total + a.cols - 1) / a.cols;
   const int64_t nvec = a.cols / VEC;
   dim3 grid(unsigned((nvec + cfg.block - 1) / cfg.block), unsigned((rows + kBgRowsPerCta - 1) / kBgRowsPerCta));
-  bias_gelu_kernel<VEC, GELU, bg_unroll<VEC>()><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
+  if constexpr (VEC == 8)
+    bias_gelu_v8_kernel<GELU, 4><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
+  else
+    bias_gelu_kernel<VEC, GELU, bg_unroll<VEC>()><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows,
+                                                                              kBgRowsPerCta);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ks::map_cuda(e);
   // The vector kernel stops at the last full VEC chunk of a ragged last row.

@@ -13,6 +13,7 @@ const char *mode_name(int m) {
     case KS_MODE_TWOPASS: return "twopass";
     case KS_MODE_STRIDED: return "strided";
     case KS_MODE_TREE: return "tree";
+    case KS_MODE_STAGED: return "staged";
     default: return "unknown";
   }
 }

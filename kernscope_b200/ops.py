@@ -51,7 +51,7 @@ def default_layernorm_config(cols: int) -> N.LayerNormConfig:
 
 def default_bias_gelu_config(cols: int, gelu: str = "tanh") -> N.BiasGeluConfig:
     vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
-    return N.BiasGeluConfig(256, vec, N.KS_GELU_TANH if gelu == "tanh" else N.KS_GELU_ERF)
+    return N.BiasGeluConfig(128, vec, N.KS_GELU_TANH if gelu == "tanh" else N.KS_GELU_ERF)
 
 
 def default_reduction_config(cols: int, axis: int) -> N.ReductionConfig:

@@ -44,7 +44,7 @@ def test_softmax_golden_all_configs(ks, path):
     r, c = fx["shape"]
     x = to_torch(fx["x"])
     ran = 0
-    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS)):
+    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS, N.KS_MODE_STAGED)):
         cfg = N.SoftmaxConfig(block, vec, mode)
         st, _ = N.validate("softmax", cfg, r, c)
         if st != 0:
@@ -91,7 +91,7 @@ def test_layernorm_golden_all_configs(ks, path):
     r, c = fx["shape"]
     x, g, b = (to_torch(fx[k]) for k in ("x", "gamma", "beta"))
     ran = 0
-    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS)):
+    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS, N.KS_MODE_STAGED)):
         cfg = N.LayerNormConfig(block, vec, mode)
         if N.validate("layernorm", cfg, r, c)[0] != 0:
             continue
