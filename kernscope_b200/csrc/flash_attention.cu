@@ -18,14 +18,20 @@
 //     MMAs of one thread execute in issue order), and each softmax warpgroup
 //     works while the tensor core runs the other tile's MMAs;
 //   * warps 0-3 / 4-7: softmax warpgroups for Q tile 0 / 1.  Thread t owns
-//     query row t: tcgen05.ld of its 128 scores, scale by log2(e)/sqrt(d),
-//     causal / length mask, running max m and sum l in registers (no
-//     shuffles), P = exp2(s - m) rounded to bf16 and written back into TMEM
-//     (columns [0,64) of its S region, two bf16 per column) as the A operand
-//     of O += P V.  O is rescaled only when the running max grows by more
-//     than 2^8 (values exp2(s - m) stay <= 256, exact in fp32/bf16 range);
-//     the final O / l is rounded to bf16 once and stored;
-//   * heavy (late) query blocks launch first for causal load balance.
+//     query row t: tcgen05.ld of its 128 scores, causal / length mask only
+//     on tiles that need it (warp-uniform test), row max with 3-input max in
+//     independent chains, P = exp2(s*log2(e)/sqrt(d) - m) with the scale
+//     folded into a packed f32x2 FMA, fp32 row sum in packed f32x2 partials,
+//     P rounded to bf16 and written back into TMEM (columns [0,64) of its S
+//     region, two bf16 per column) as the A operand of O += P V.  The pipeline
+//     period is (softmax time + one P V and one Q K^T MMA), so the softmax's
+//     issue count per element is what bounds the tensor-core utilisation.  O
+//     is rescaled only when the running max grows by more than 2^8 (values
+//     exp2(s - m) stay <= 256, exact in fp32/bf16 range); the final O / l is
+//     rounded to bf16 once and stored;
+//   * causal: tile 0 stops one K/V tile before tile 1 (its last tile is fully
+//     masked) and its epilogue starts while tile 1's last MMAs run; heavy
+//     (late) query blocks launch first for load balance.
 //
 // All waits are bounded (KsWait); teardown waits for outstanding TMA loads
 // and MMAs before TMEM is freed.
@@ -42,13 +48,14 @@ constexpr uint32_t kBox = 128 * 64 * 2;  // [128 rows x 64 cols] bf16 box = 16 K
 constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
 constexpr int kStages = 2;
 
+
 struct FaLayout {
   static constexpr uint32_t q_off = 0;                           // Q0, Q1
   static constexpr uint32_t k_off = q_off + 2 * kTileBytes;      // K[stages]
   static constexpr uint32_t v_off = k_off + kStages * kTileBytes;  // V[stages]
   static constexpr uint32_t bar_off = v_off + kStages * kTileBytes;
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full, drain
-  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 1 + 1;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain
+  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t smem_request = bytes + 1024;
@@ -58,6 +65,37 @@ KS_DEV float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+KS_DEV float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic: one instruction, two
+// lanes' worth of FFMA/FADD), used to halve the issue cost of the softmax.
+struct F2 {
+  float x, y;
+};
+KS_DEV F2 fma2(F2 a, F2 b, F2 c) {
+  F2 d;
+  asm("{\n\t.reg .b64 A, B, C, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
+      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+KS_DEV F2 add2(F2 a, F2 b) {
+  F2 d;
+  asm("{\n\t.reg .b64 A, B, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "add.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
 }
 
 KS_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -113,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *s_full = bars + 1 + 3 * kStages;
   uint64_t *p_full = s_full + 2;
   uint64_t *o_full = p_full + 2;
-  uint64_t *drain = o_full + 1;
+  uint64_t *drain = o_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
 
@@ -124,9 +162,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = qb * 2 * kTile;
   // number of K/V tiles this block needs
   int n_kv = (nk + kTile - 1) / kTile;
+  // tile g needs K/V tiles [0, n_t[g]); n_kv = n_t[1] >= n_t[0].  Under the
+  // causal mask tile 0 stops one K/V tile earlier (its last one is masked).
+  int n_t[2] = {n_kv, n_kv};
   if (causal) {
+    n_t[0] = min(n_kv, (q0 + kTile - 1) / kTile + 1);
     const int q_last = min(q0 + 2 * kTile, nq) - 1;
     n_kv = min(n_kv, q_last / kTile + 1);
+    n_t[1] = n_kv;
+    n_t[0] = min(n_t[0], n_kv);
   }
 
   if (threadIdx.x == 0) {
@@ -140,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ks_mbar_init(s_full + g, 1);
       ks_mbar_init(p_full + g, 4);
     }
-    ks_mbar_init(o_full, 1);
+    ks_mbar_init(o_full + 0, 1);
+    ks_mbar_init(o_full + 1, 1);
     ks_mbar_init(drain, 1);
     *abort = 0;
     ks_fence_mbar_init();
@@ -208,15 +253,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (j / kStages) & 1;
         const int st1 = (j + 1) % kStages;
         const uint32_t ph1 = ((j + 1) / kStages) & 1;
-        const bool more = j + 1 < n_kv;
+        const bool more0 = j + 1 < n_t[0], more1 = j + 1 < n_kv;
         if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
         // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
-        if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
-        ks_tc_fence_after();
-        issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
-        if (more) {
+        if (j < n_t[0]) {
+          if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
+          ks_tc_fence_after();
+          issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
+          if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
+        }
+        if (more1) {
           if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
           ks_tc_fence_after();
+        }
+        if (more0) {
           issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
           ks_umma_commit(s_full + 0);
         }
@@ -225,12 +275,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ks_tc_fence_after();
         issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0);
         ks_umma_commit(kv_empty + st);
-        if (more) {
+        if (more1) {
           issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
           ks_umma_commit(s_full + 1);
+        } else {
+          ks_umma_commit(o_full + 1);
         }
       }
-      ks_umma_commit(o_full);
       ks_umma_commit(drain);
       ks_mbar_wait(drain, 0, nullptr, wait);
     }
@@ -244,31 +295,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_col = g * 128, o_col = 256 + g * 128;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    const int n_mine = n_t[g];
+    for (int j = 0; j < n_mine; ++j) {
       if (!ks_mbar_wait(s_full + g, j & 1, abort, wait)) {
         ok = false;
         break;
       }
       ks_tc_fence_after();
       uint32_t r[128];
-      ks_tmem_ld32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      ks_tmem_ld32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      ks_tmem_ld32(lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      ks_tmem_ld32(lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      ks_tmem_ld32_at<0>(lane_addr + s_col + 0, r);
+      ks_tmem_ld32_at<32>(lane_addr + s_col + 32, r);
+      ks_tmem_ld32_at<64>(lane_addr + s_col + 64, r);
+      ks_tmem_ld32_at<96>(lane_addr + s_col + 96, r);
       ks_tmem_wait_ld();
       const int kv0 = j * kTile;
       // keys beyond this row's limit are masked: causal (key > query) and length
       int lim = nk - kv0;  // number of valid keys in this tile
       if (causal) lim = min(lim, qrow - kv0 + 1);
-      float mx = -INFINITY;
+      // warp-uniform: most tiles are unmasked for all 32 rows of the warp
+      const bool full_tile = __all_sync(0xffffffffu, lim >= kTile);
+      if (!full_tile) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float s = __uint_as_float(r[c]) * scale_log2;
-        s = c < lim ? s : -INFINITY;
-        r[c] = __float_as_uint(s);
-        mx = fmaxf(mx, s);
+        for (int c = 0; c < 128; ++c)
+          if (c >= lim) r[c] = 0xff800000u;  // -inf
       }
-      const float m_new = fmaxf(m, mx);
+      // row max of the raw scores (scale > 0 commutes with max), as four
+      // independent chains of 3-input max so latency does not serialise
+      float mm[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        mm[u] = max3(__uint_as_float(r[u]), __uint_as_float(r[u + 4]), __uint_as_float(r[u + 8]));
+#pragma unroll
+      for (int c = 12; c < 124; c += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mm[u] = max3(mm[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 4 + u]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mm[u] = fmaxf(mm[u], __uint_as_float(r[124 + u]));
+      const float mx = fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3]));
+      const float m_new = fmaxf(m, mx * scale_log2);
       const bool grow = m_new > m + 8.f;  // also true on the first finite max
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O has absorbed every earlier P V (the S commit follows it), rescale.
@@ -288,27 +352,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= ex2(m - m_new);
         m = m_new;
       }
-      const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
-      uint32_t p[64];
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
+      const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
+      // P in two halves of 64 keys (32 packed columns each), stored as soon as
+      // computed: the S columns they overwrite are already in registers
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float a = ex2(__uint_as_float(r[2 * c]) - mu);
-        const float b = ex2(__uint_as_float(r[2 * c + 1]) - mu);
-        p[c] = ks_pack_bf16x2(a, b);
-        // the sum uses the bf16-rounded P that the MMA consumes
-        rs += ks_bf16_lo(p[c]) + ks_bf16_hi(p[c]);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t p[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int e0 = 64 * half + 2 * c;
+          // exponent pair x = s*scale_log2 - m as one packed FFMA
+          const F2 x = fma2(F2{__uint_as_float(r[e0]), __uint_as_float(r[e0 + 1])}, sc2, nm2);
+          const F2 e{ex2(x.x), ex2(x.y)};
+          rsum[c & 3] = add2(rsum[c & 3], e);
+          p[c] = ks_pack_bf16x2(e.x, e.y);
+        }
+        if (half == 0)
+          ks_tmem_st32_at<0>(lane_addr + s_col + 0, p);
+        else
+          ks_tmem_st32_at<0>(lane_addr + s_col + 32, p);
       }
+      const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
+      const float rs = rs2.x + rs2.y;
       l += rs;
-      tmem_st32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&p[0]));
-      tmem_st32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&p[32]));
       ks_tmem_wait_st();
       ks_tc_fence_before();
       __syncwarp();
       if (lane == 0) ks_mbar_arrive(p_full + g);
     }
     // epilogue: O / l -> bf16 -> out[bh, qrow, :]
-    if (ok && ks_mbar_wait(o_full, 0, abort, wait)) {
+    if (ok && ks_mbar_wait(o_full + g, 0, abort, wait)) {
       ks_tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint16_t *dst = out + (int64_t(bh) * nq + qrow) * kD;
