@@ -86,7 +86,10 @@ def build_tuner(force: bool) -> None:
     hdrs = sorted(glob.glob(os.path.join(HOST, "*.h"))) + [os.path.join(INCLUDE, "kernscope_b200.h")]
     lib_srcs = [s for s in srcs if not s.endswith("tune_cli.cpp")]
     cli_src = [s for s in srcs if s.endswith("tune_cli.cpp")]
-    cxx = os.environ.get("CXX", "g++")
+    # The system g++ (nvcc's host compiler): both libraries must share one
+    # dynamic libstdc++ (a toolchain that links libstdc++ statically would put
+    # a second copy in the process next to the one the kernel library uses).
+    cxx = os.environ.get("KS_CXX", "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++")
     common = ["-std=c++20", "-O2", "-fPIC", "-Wall", "-I", INCLUDE, "-I", HOST]
     rpath = "-Wl,-rpath,$ORIGIN"
     if force or _newer(TUNE_LIB, lib_srcs + hdrs + [KERNEL_LIB]):

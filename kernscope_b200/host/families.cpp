@@ -1,0 +1,1031 @@
+// families.cpp -- config spaces, validation, sessions and gate references of
+// the six kernel families.
+#include "families.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <sstream>
+
+#include "hwmodel.h"
+
+namespace kernscope::tune {
+
+// ---------------------------------------------------------------------------
+// bf16, seeded inputs, device buffers
+// ---------------------------------------------------------------------------
+std::uint16_t f32_to_bf16(float f) {
+  std::uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return std::uint16_t((u >> 16) | 0x40u);  // NaN stays NaN
+  const std::uint32_t rounding = 0x7fffu + ((u >> 16) & 1u);                    // round to nearest even
+  return std::uint16_t((u + rounding) >> 16);
+}
+float bf16_to_f32(std::uint16_t h) {
+  const std::uint32_t u = std::uint32_t(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+static float rbf(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+namespace {
+
+// splitmix64 stream -> uniform doubles in [lo, hi)
+struct Rng {
+  std::uint64_t s;
+  explicit Rng(std::uint64_t seed) : s(seed * 0x9E3779B97F4A7C15ull + 0x632BE59BD9B4E019ull) {}
+  std::uint64_t next() {
+    std::uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  }
+  double uniform(double lo, double hi) { return lo + (hi - lo) * double(next() >> 11) * 0x1.0p-53; }
+};
+
+// bf16 tensor with host copy (bf16 bits + fp32 view) and a device copy
+struct DevBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf &) = delete;
+  DevBuf &operator=(const DevBuf &) = delete;
+  ~DevBuf() {
+    if (p) ks_gpu_free(p);
+  }
+  int alloc(size_t n) {
+    bytes = n;
+    return ks_gpu_malloc(&p, n < 256 ? 256 : n);
+  }
+};
+
+struct HostBf16 {
+  std::vector<std::uint16_t> bits;
+  std::vector<float> f;
+  void fill_uniform(Rng &r, size_t n, double lo, double hi) {
+    bits.resize(n);
+    f.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+      bits[i] = f32_to_bf16(float(r.uniform(lo, hi)));
+      f[i] = bf16_to_f32(bits[i]);
+    }
+  }
+};
+
+int upload(DevBuf &d, const void *src, size_t bytes) {
+  int s = d.alloc(bytes);
+  if (s == KS_OK && bytes > 0) s = ks_gpu_memcpy_htod(d.p, src, bytes, nullptr);
+  if (s == KS_OK) s = ks_gpu_synchronize();
+  return s;
+}
+
+int download_bf16(const DevBuf &d, size_t n, std::vector<float> *out) {
+  std::vector<std::uint16_t> h(n);
+  int s = ks_gpu_memcpy_dtoh(h.data(), d.p, n * 2, nullptr);
+  if (s == KS_OK) s = ks_gpu_synchronize();
+  out->resize(n);
+  for (size_t i = 0; i < n; ++i) (*out)[i] = bf16_to_f32(h[i]);
+  return s;
+}
+
+int iget(const json &c, const char *k, int d) { return int(c.number_or(k, d)); }
+
+std::string shape_str(const std::vector<std::int64_t> &s) {
+  std::string o;
+  for (size_t i = 0; i < s.size(); ++i) o += (i ? "," : "") + std::to_string(s[i]);
+  return o;
+}
+
+bool valid_elem_shape(const std::vector<std::int64_t> &s, std::string *r, const char *fam) {
+  if (s.size() != 2 || s[0] <= 0 || s[1] <= 0) {
+    if (r) *r = std::string(fam) + " expects --shape R,C (positive)";
+    return false;
+  }
+  return true;
+}
+
+int mode_from(const json &c, int dflt) {
+  const std::string s = c.string_or("mode", "");
+  if (s == "onepass") return KS_MODE_ONEPASS;
+  if (s == "twopass") return KS_MODE_TWOPASS;
+  if (s == "strided") return KS_MODE_STRIDED;
+  if (s == "tree") return KS_MODE_TREE;
+  if (s == "staged") return KS_MODE_STAGED;
+  return dflt;
+}
+
+}  // namespace
+
+const char *elem_mode_name(ElemMode m) noexcept {
+  switch (m) {
+    case ElemMode::kOnePass: return "onepass";
+    case ElemMode::kTwoPass: return "twopass";
+    case ElemMode::kStrided: return "strided";
+    case ElemMode::kTree: return "tree";
+    case ElemMode::kStaged: return "staged";
+  }
+  return "unknown";
+}
+
+std::string canonical_config(const json &cfg) {
+  if (!cfg.is_object()) return cfg.dump();
+  std::vector<std::pair<std::string, std::string>> kv;
+  for (const auto &[k, v] : cfg.as_object()) kv.emplace_back(k, v.dump());
+  std::sort(kv.begin(), kv.end());
+  std::string s = "{";
+  for (size_t i = 0; i < kv.size(); ++i) s += (i ? "," : "") + kv[i].first + ":" + kv[i].second;
+  return s + "}";
+}
+
+// ---------------------------------------------------------------------------
+// verdicts
+// ---------------------------------------------------------------------------
+GateVerdict bf16_verdict(const std::vector<float> &a, const std::vector<float> &r) {
+  GateVerdict v;
+  const size_t n = std::min(a.size(), r.size());
+  double dot = 0, na = 0, nr = 0, ma = 0, mr = 0, mre = 0, ss = 0, se = 0;
+  for (size_t i = 0; i < n; ++i) {
+    dot += double(a[i]) * r[i];
+    na += double(a[i]) * a[i];
+    nr += double(r[i]) * r[i];
+    ma += a[i];
+    mr += r[i];
+    mre = std::max(mre, std::fabs(double(a[i]) - r[i]) / (std::fabs(double(r[i])) + 1e-6));
+  }
+  v.cosine = (na > 0 && nr > 0) ? dot / std::sqrt(na * nr) : (na == 0 && nr == 0 ? 1.0 : 0.0);
+  v.max_rel_err = mre;
+  ma /= double(std::max<size_t>(n, 1));
+  mr /= double(std::max<size_t>(n, 1));
+  double sxy = 0, sxx = 0, syy = 0;
+  for (size_t i = 0; i < n; ++i) {
+    sxy += (a[i] - ma) * (r[i] - mr);
+    sxx += (a[i] - ma) * (a[i] - ma);
+    syy += (r[i] - mr) * (r[i] - mr);
+  }
+  v.pcc = (sxx > 0 && syy > 0) ? sxy / std::sqrt(sxx * syy) : 1.0;
+  const double rms = std::sqrt(nr / double(std::max<size_t>(n, 1)));
+  double fmax = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const double den = std::max(std::fabs(double(r[i])), rms * std::ldexp(1.0, -8));
+    const double e = std::fabs(double(a[i]) - r[i]);
+    se += e * e;
+    ss += double(r[i]) * r[i];
+    if (den > 0) fmax = std::max(fmax, e / den);
+  }
+  v.floor_rel_err = fmax;
+  v.norm_rel_err = ss > 0 ? std::sqrt(se / ss) : std::sqrt(se);
+  v.pass = v.cosine >= 0.999 && v.pcc >= 0.99 && v.floor_rel_err <= 1e-2 && v.norm_rel_err <= 1e-2;
+  v.criterion = "cosine>=0.999, pcc>=0.99, floor rel-err<=1e-2, norm rel-err<=1e-2";
+  return v;
+}
+
+GateVerdict Session::verdict(const std::vector<float> &got, const std::vector<float> &ref) const {
+  return bf16_verdict(got, ref);
+}
+
+// ===========================================================================
+// matmul
+// ===========================================================================
+namespace {
+ks_matmul_config to_mm(const json &c) {
+  return ks_matmul_config{iget(c, "tile_m", 128), iget(c, "tile_n", 256), iget(c, "tile_k", 64),
+                          iget(c, "stages", 4),   iget(c, "acc_stages", 2), iget(c, "group_m", 8)};
+}
+json mm_json(int bn, int st, int acc, int g) {
+  return db::json::object({{"tile_m", json(128)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
+                           {"stages", json(st)}, {"acc_stages", json(acc)}, {"group_m", json(g)}});
+}
+int pow2_cols(int c) {
+  int p = 32;
+  while (p < c) p <<= 1;
+  return p;
+}
+
+class MatmulSession : public Session {
+ public:
+  std::int64_t m, n, k;
+  HostBf16 a, b;
+  DevBuf da, db, dc;
+  int init(std::int64_t M, std::int64_t N, std::int64_t K, std::uint64_t seed) {
+    m = M, n = N, k = K;
+    Rng r(seed);
+    a.fill_uniform(r, size_t(m * k), -1, 1);
+    b.fill_uniform(r, size_t(k * n), -1, 1);
+    int s = upload(da, a.bits.data(), a.bits.size() * 2);
+    if (s == KS_OK) s = upload(db, b.bits.data(), b.bits.size() * 2);
+    if (s == KS_OK) s = dc.alloc(size_t(m * n) * 2);
+    return s;
+  }
+  int launch(const json &cfg, void *st) override {
+    ks_matmul_config c = to_mm(cfg);
+    ks_matmul_args args{da.p, db.p, dc.p, m, n, k};
+    return ks_matmul_launch(&c, &args, st);
+  }
+  int output(std::vector<float> *o) override { return download_bf16(dc, size_t(m * n), o); }
+  void reference(std::vector<float> *o) const override {
+    o->assign(size_t(m * n), 0.f);
+    std::vector<float> acc(static_cast<size_t>(n));
+    for (std::int64_t i = 0; i < m; ++i) {
+      std::fill(acc.begin(), acc.end(), 0.f);
+      for (std::int64_t kk = 0; kk < k; ++kk) {
+        const float av = a.f[size_t(i * k + kk)];
+        const float *brow = &b.f[size_t(kk * n)];
+        for (std::int64_t j = 0; j < n; ++j) acc[size_t(j)] += av * brow[j];
+      }
+      for (std::int64_t j = 0; j < n; ++j) (*o)[size_t(i * n + j)] = rbf(acc[size_t(j)]);
+    }
+  }
+  int corrupt_output(void *st) override { return ks_gpu_memset(dc.p, 0, size_t(m * n) * 2, st); }
+};
+
+class MatmulFamily : public Family {
+ public:
+  const char *name() const override { return "matmul"; }
+  bool check_shape(const std::vector<std::int64_t> &s, std::string *r) const override {
+    if (s.size() != 3 || s[0] <= 0 || s[1] <= 0 || s[2] <= 0) {
+      if (r) *r = "matmul expects --shape M,N,K (positive)";
+      return false;
+    }
+    return true;
+  }
+  std::vector<json> enumerate(bool full, const std::vector<std::int64_t> &) const override {
+    std::vector<json> v;
+    if (!full) {
+      for (auto [bn, st] : {std::pair{256, 3}, {256, 4}, {128, 4}, {128, 6}})
+        for (int acc : {1, 2})
+          for (int g : {8, 16}) v.push_back(mm_json(bn, st, acc, g));
+      return v;
+    }
+    for (int bn : {64, 128, 256})
+      for (int st = 2; st <= 6; ++st)
+        for (int acc : {1, 2})
+          for (int g : {1, 4, 8, 16, 32}) v.push_back(mm_json(bn, st, acc, g));
+    return v;
+  }
+  ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
+    MatmulConfig c{iget(cfg, "tile_m", 0), iget(cfg, "tile_n", 0), iget(cfg, "tile_k", 0), iget(cfg, "stages", 0),
+                   iget(cfg, "acc_stages", 0), iget(cfg, "group_m", 0)};
+    return validate_config(c, MatmulProblem{s[0], s[1], s[2], arch, 2});
+  }
+  Resources resources(const json &cfg, const std::vector<std::int64_t> &) const override {
+    ks_matmul_config c = to_mm(cfg);
+    return Resources{64, int(smem_bytes(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m})),
+                     192, pow2_cols(c.acc_stages * c.tile_n)};
+  }
+  LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    ks_matmul_config c = to_mm(cfg);
+    return launch_geometry(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m},
+                           MatmulProblem{s[0], s[1], s[2], "sm_100a", 2});
+  }
+  std::string symbol(const json &cfg) const override {
+    ks_matmul_config c = to_mm(cfg);
+    return kernel_symbol(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m});
+  }
+  std::vector<std::int64_t> gate_shape(const std::vector<std::int64_t> &) const override { return {64, 64, 64}; }
+  std::int64_t flops(const std::vector<std::int64_t> &s, const json &) const override {
+    return roofline::compute_flops(roofline::KernelFamily::kGemm, {s[0], s[1], s[2], 0, 2});
+  }
+  std::int64_t bytes(const std::vector<std::int64_t> &s) const override {
+    return roofline::compute_bytes_moved(roofline::KernelFamily::kGemm, {s[0], s[1], s[2], 0, 2});
+  }
+  std::unique_ptr<Session> make_session(const std::vector<std::int64_t> &s, std::uint64_t seed,
+                                        std::string *err) const override {
+    auto p = std::make_unique<MatmulSession>();
+    const int st = p->init(s[0], s[1], s[2], seed);
+    if (st != KS_OK) {
+      if (err) *err = std::string("matmul session: ") + ks_status_string(st);
+      return nullptr;
+    }
+    return p;
+  }
+  std::string generate_source(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    ks_matmul_config c = to_mm(cfg);
+    std::ostringstream o;
+    o << "// reproducer: " << symbol(cfg) << " at M,N,K = " << shape_str(s) << "\n"
+      << "#include <kernscope_b200.h>\n#include <cstdio>\n#include <vector>\n"
+      << "int main() {\n  const long long m = " << s[0] << ", n = " << s[1] << ", k = " << s[2] << ";\n"
+      << "  void *a, *b, *c;\n  ks_gpu_malloc(&a, m * k * 2); ks_gpu_malloc(&b, k * n * 2); ks_gpu_malloc(&c, m * n * 2);\n"
+      << "  ks_gpu_memset(a, 0, m * k * 2, nullptr); ks_gpu_memset(b, 0, k * n * 2, nullptr);\n"
+      << "  ks_matmul_config cfg{" << c.tile_m << ", " << c.tile_n << ", " << c.tile_k << ", " << c.stages << ", "
+      << c.acc_stages << ", " << c.group_m << "};\n"
+      << "  ks_matmul_args args{a, b, c, m, n, k};\n"
+      << "  int st = ks_matmul_launch(&cfg, &args, nullptr);\n  if (st == 0) st = ks_gpu_synchronize();\n"
+      << "  std::printf(\"%s\\n\", ks_status_string(st));\n  return st == 0 ? 0 : 1;\n}\n";
+    return o.str();
+  }
+};
+
+// ===========================================================================
+// flash attention
+// ===========================================================================
+// shapes: Nq,Nk,d (one head, the reference ABI) or B,H,N,d (self-attention)
+struct FaShape {
+  std::int64_t bh, nq, nk, d;
+};
+FaShape fa_shape(const std::vector<std::int64_t> &s) {
+  if (s.size() == 4) return {s[0] * s[1], s[2], s[2], s[3]};
+  return {1, s[0], s[1], s[2]};
+}
+
+class FlashSession : public Session {
+ public:
+  FaShape sh;
+  bool causal = false;
+  HostBf16 q, k, v;
+  DevBuf dq, dk, dv, dout;
+  int init(const FaShape &s, bool c, std::uint64_t seed) {
+    sh = s;
+    causal = c;
+    Rng r(seed);
+    const double sc = 1.0 / std::sqrt(double(s.d));  // the reference profile (inputs.py:98-105)
+    q.fill_uniform(r, size_t(s.bh * s.nq * s.d), -sc, sc);
+    k.fill_uniform(r, size_t(s.bh * s.nk * s.d), -sc, sc);
+    v.fill_uniform(r, size_t(s.bh * s.nk * s.d), -1, 1);
+    int st = upload(dq, q.bits.data(), q.bits.size() * 2);
+    if (st == KS_OK) st = upload(dk, k.bits.data(), k.bits.size() * 2);
+    if (st == KS_OK) st = upload(dv, v.bits.data(), v.bits.size() * 2);
+    if (st == KS_OK) st = dout.alloc(q.bits.size() * 2);
+    return st;
+  }
+  int launch(const json &cfg, void *st) override {
+    ks_flash_attention_config c{iget(cfg, "tile_m", 128), iget(cfg, "tile_n", 128), iget(cfg, "stages", 2),
+                                causal ? 1 : 0};
+    ks_flash_attention_args a{dq.p, dk.p, dv.p, dout.p, 1, sh.bh, sh.nq, sh.nk, sh.d, 0.f};
+    return ks_flash_attention_launch(&c, &a, st);
+  }
+  int output(std::vector<float> *o) override { return download_bf16(dout, size_t(sh.bh * sh.nq * sh.d), o); }
+  void reference(std::vector<float> *o) const override {
+    o->assign(size_t(sh.bh * sh.nq * sh.d), 0.f);
+    const float scale = 1.f / std::sqrt(float(sh.d));
+    std::vector<float> srow(static_cast<size_t>(sh.nk)), acc(static_cast<size_t>(sh.d));
+    for (std::int64_t h = 0; h < sh.bh; ++h)
+      for (std::int64_t i = 0; i < sh.nq; ++i) {
+        const float *qi = &q.f[size_t((h * sh.nq + i) * sh.d)];
+        float mx = -INFINITY;
+        for (std::int64_t j = 0; j < sh.nk; ++j) {
+          if (causal && j > i) {
+            srow[size_t(j)] = -INFINITY;
+            continue;
+          }
+          const float *kj = &k.f[size_t((h * sh.nk + j) * sh.d)];
+          float s = 0.f;
+          for (std::int64_t c = 0; c < sh.d; ++c) s += qi[c] * kj[c];
+          srow[size_t(j)] = s * scale;
+          mx = std::max(mx, srow[size_t(j)]);
+        }
+        float sum = 0.f;
+        for (std::int64_t j = 0; j < sh.nk; ++j) {
+          srow[size_t(j)] = std::exp(srow[size_t(j)] - mx);
+          sum += srow[size_t(j)];
+        }
+        std::fill(acc.begin(), acc.end(), 0.f);
+        for (std::int64_t j = 0; j < sh.nk; ++j) {
+          const float p = srow[size_t(j)] / sum;
+          if (p == 0.f) continue;
+          const float *vj = &v.f[size_t((h * sh.nk + j) * sh.d)];
+          for (std::int64_t c = 0; c < sh.d; ++c) acc[size_t(c)] += p * vj[c];
+        }
+        for (std::int64_t c = 0; c < sh.d; ++c) (*o)[size_t((h * sh.nq + i) * sh.d + c)] = rbf(acc[size_t(c)]);
+      }
+  }
+  // The tensor-core path rounds P to bf16 before P V (2^-9 per probability):
+  // per element |a - r| <= 1e-2 * rho, rho = softmax |V| (row weights of |V|).
+  GateVerdict verdict(const std::vector<float> &got, const std::vector<float> &ref) const override {
+    GateVerdict gv = bf16_verdict(got, ref);
+    if (sh.d != 128) return gv;
+    double worst = 0.0;
+    const float scale = 1.f / std::sqrt(float(sh.d));
+    std::vector<float> srow(static_cast<size_t>(sh.nk));
+    for (std::int64_t h = 0; h < sh.bh; ++h)
+      for (std::int64_t i = 0; i < sh.nq; ++i) {
+        const float *qi = &q.f[size_t((h * sh.nq + i) * sh.d)];
+        float mx = -INFINITY;
+        for (std::int64_t j = 0; j < sh.nk; ++j) {
+          float s = -INFINITY;
+          if (!(causal && j > i)) {
+            const float *kj = &k.f[size_t((h * sh.nk + j) * sh.d)];
+            s = 0.f;
+            for (std::int64_t c = 0; c < sh.d; ++c) s += qi[c] * kj[c];
+            s *= scale;
+          }
+          srow[size_t(j)] = s;
+          mx = std::max(mx, s);
+        }
+        double sum = 0;
+        for (auto &x : srow) {
+          x = std::exp(x - mx);
+          sum += x;
+        }
+        for (std::int64_t c = 0; c < sh.d; ++c) {
+          double rho = 0;
+          for (std::int64_t j = 0; j < sh.nk; ++j) rho += srow[size_t(j)] * std::fabs(v.f[size_t((h * sh.nk + j) * sh.d + c)]);
+          rho /= sum;
+          const size_t idx = size_t((h * sh.nq + i) * sh.d + c);
+          if (rho > 0) worst = std::max(worst, std::fabs(double(got[idx]) - ref[idx]) / rho);
+        }
+      }
+    gv.floor_rel_err = worst;
+    gv.pass = gv.cosine >= 0.999 && gv.pcc >= 0.99 && worst <= 1e-2 && gv.norm_rel_err <= 1e-2;
+    gv.criterion = "cosine>=0.999, pcc>=0.99, |a-r| <= 1e-2 * softmax|V|, norm rel-err<=1e-2";
+    return gv;
+  }
+  int corrupt_output(void *st) override { return ks_gpu_memset(dout.p, 0, dout.bytes, st); }
+};
+
+class FlashFamily : public Family {
+ public:
+  bool causal = false;
+  const char *name() const override { return "flash_attention"; }
+  bool check_shape(const std::vector<std::int64_t> &s, std::string *r) const override {
+    if ((s.size() != 3 && s.size() != 4) || std::any_of(s.begin(), s.end(), [](auto x) { return x <= 0; })) {
+      if (r) *r = "flash_attention expects --shape Nq,Nk,d or B,H,N,d (positive)";
+      return false;
+    }
+    return true;
+  }
+  std::vector<json> enumerate(bool, const std::vector<std::int64_t> &) const override {
+    // TMEM holds exactly two 128x128 S tiles and two 128x128 O tiles (512
+    // columns): the sm_100a space is the 128x128 tile with a 2-stage ring.
+    return {db::json::object({{"tile_m", json(128)}, {"tile_n", json(128)}, {"stages", json(2)},
+                              {"causal", json(causal)}})};
+  }
+  ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
+    const FaShape f = fa_shape(s);
+    FlashAttentionConfig c{iget(cfg, "tile_m", 0), iget(cfg, "tile_n", 0), iget(cfg, "stages", 0),
+                           cfg.find("causal") && cfg.find("causal")->as_bool()};
+    return validate_config(c, FlashAttentionProblem{f.nq, f.nk, f.d, f.bh, causal, arch, 2});
+  }
+  Resources resources(const json &, const std::vector<std::int64_t> &s) const override {
+    const FaShape f = fa_shape(s);
+    if (f.d != 128) return Resources{48, 4 * 256 * 4, 128, 0};
+    return Resources{168, int(smem_bytes(FlashAttentionConfig{}, FlashAttentionProblem{})), 320, 512};
+  }
+  LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    const FaShape f = fa_shape(s);
+    return launch_geometry(FlashAttentionConfig{128, 128, 2, causal},
+                           FlashAttentionProblem{f.nq, f.nk, f.d, f.bh, causal, "sm_100a", 2});
+    (void)cfg;
+  }
+  std::string symbol(const json &) const override { return kernel_symbol(FlashAttentionConfig{128, 128, 2, causal}); }
+  std::vector<std::int64_t> gate_shape(const std::vector<std::int64_t> &s) const override {
+    const FaShape f = fa_shape(s);
+    return {1, 2, std::min<std::int64_t>(std::max(f.nq, f.nk), 256), f.d};
+  }
+  std::int64_t flops(const std::vector<std::int64_t> &s, const json &) const override {
+    const FaShape f = fa_shape(s);
+    roofline::Shape r{f.bh, f.nq, 0, f.d, 2, causal};
+    return roofline::compute_flops(roofline::KernelFamily::kFlashAttention, r);
+  }
+  std::int64_t bytes(const std::vector<std::int64_t> &s) const override {
+    const FaShape f = fa_shape(s);
+    return 2 * f.bh * (2 * f.nq + 2 * f.nk) * f.d;
+  }
+  std::unique_ptr<Session> make_session(const std::vector<std::int64_t> &s, std::uint64_t seed,
+                                        std::string *err) const override {
+    auto p = std::make_unique<FlashSession>();
+    const int st = p->init(fa_shape(s), causal, seed);
+    if (st != KS_OK) {
+      if (err) *err = std::string("flash_attention session: ") + ks_status_string(st);
+      return nullptr;
+    }
+    return p;
+  }
+  std::string generate_source(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    const FaShape f = fa_shape(s);
+    std::ostringstream o;
+    o << "// reproducer: " << symbol(cfg) << " at (B*H, Nq, Nk, d) = (" << f.bh << ", " << f.nq << ", " << f.nk
+      << ", " << f.d << ")\n#include <kernscope_b200.h>\n#include <cstdio>\n"
+      << "int main() {\n  const long long bh = " << f.bh << ", nq = " << f.nq << ", nk = " << f.nk << ", d = " << f.d
+      << ";\n  void *q, *k, *v, *o;\n"
+      << "  ks_gpu_malloc(&q, bh * nq * d * 2); ks_gpu_malloc(&k, bh * nk * d * 2); ks_gpu_malloc(&v, bh * nk * d * 2);\n"
+      << "  ks_gpu_malloc(&o, bh * nq * d * 2);\n"
+      << "  ks_gpu_memset(q, 0, bh * nq * d * 2, nullptr); ks_gpu_memset(k, 0, bh * nk * d * 2, nullptr);\n"
+      << "  ks_gpu_memset(v, 0, bh * nk * d * 2, nullptr);\n"
+      << "  ks_flash_attention_config cfg{128, 128, 2, " << (causal ? 1 : 0) << "};\n"
+      << "  ks_flash_attention_args args{q, k, v, o, 1, bh, nq, nk, d, 0.f};\n"
+      << "  int st = ks_flash_attention_launch(&cfg, &args, nullptr);\n  if (st == 0) st = ks_gpu_synchronize();\n"
+      << "  std::printf(\"%s\\n\", ks_status_string(st));\n  return st == 0 ? 0 : 1;\n}\n";
+    return o.str();
+  }
+};
+
+// ===========================================================================
+// row ops (softmax, layernorm, bias_gelu) and reduction
+// ===========================================================================
+enum class RowKind { kSoftmax, kLayerNorm, kBiasGelu, kReduction };
+
+class RowSession : public Session {
+ public:
+  RowKind kind;
+  std::int64_t rows = 0, cols = 0;
+  int gelu = KS_GELU_ERF;
+  int axis = 0;  // reduction
+  HostBf16 x, p1, p2;
+  std::vector<float> xf32;  // reduction full sum input
+  DevBuf dx, dp1, dp2, dout, dws;
+  size_t out_n = 0;
+
+  int init(RowKind k, std::int64_t r, std::int64_t c, int g, int ax, std::uint64_t seed) {
+    kind = k;
+    rows = r;
+    cols = c;
+    gelu = g;
+    axis = ax;
+    Rng rng(seed);
+    int st = KS_OK;
+    const size_t n = size_t(r * c);
+    // distributions of the reference profile (inputs.py:77-97)
+    switch (k) {
+      case RowKind::kSoftmax: x.fill_uniform(rng, n, -2, 2); break;
+      case RowKind::kLayerNorm:
+        x.fill_uniform(rng, n, -1, 1);
+        p1.fill_uniform(rng, size_t(c), 0.5, 1.5);
+        p2.fill_uniform(rng, size_t(c), -0.25, 0.25);
+        break;
+      case RowKind::kBiasGelu:
+        x.fill_uniform(rng, n, -1, 1);
+        p1.fill_uniform(rng, size_t(c), -0.25, 0.25);
+        break;
+      case RowKind::kReduction:
+        if (axis == -1) {
+          xf32.resize(n);
+          for (auto &v : xf32) v = float(rng.uniform(0, 1));
+        } else {
+          x.fill_uniform(rng, n, -1, 1);
+        }
+        break;
+    }
+    if (k == RowKind::kReduction && axis == -1)
+      st = upload(dx, xf32.data(), n * 4);
+    else
+      st = upload(dx, x.bits.data(), n * 2);
+    if (st == KS_OK && !p1.bits.empty()) st = upload(dp1, p1.bits.data(), p1.bits.size() * 2);
+    if (st == KS_OK && !p2.bits.empty()) st = upload(dp2, p2.bits.data(), p2.bits.size() * 2);
+    out_n = k == RowKind::kReduction ? (axis == -1 ? 1 : size_t(c)) : n;
+    const size_t out_bytes = k == RowKind::kReduction && axis == -1 ? 4 : out_n * 2;
+    if (st == KS_OK) st = dout.alloc(out_bytes);
+    return st;
+  }
+
+  int launch(const json &cfg, void *st) override {
+    const int block = iget(cfg, "block", 256), vec = iget(cfg, "vec_width", 8);
+    switch (kind) {
+      case RowKind::kSoftmax: {
+        ks_softmax_config c{block, vec, mode_from(cfg, KS_MODE_ONEPASS)};
+        ks_softmax_args a{dx.p, dout.p, rows, cols};
+        return ks_softmax_launch(&c, &a, st);
+      }
+      case RowKind::kLayerNorm: {
+        ks_layernorm_config c{block, vec, mode_from(cfg, KS_MODE_ONEPASS)};
+        ks_layernorm_args a{dx.p, dp1.p, dp2.p, dout.p, rows, cols, 1e-5f};
+        return ks_layernorm_launch(&c, &a, st);
+      }
+      case RowKind::kBiasGelu: {
+        ks_bias_gelu_config c{block, vec, gelu};
+        ks_bias_gelu_args a{dx.p, dp1.p, dout.p, rows * cols, cols};
+        return ks_bias_gelu_launch(&c, &a, st);
+      }
+      case RowKind::kReduction: {
+        ks_reduction_config c{block, vec, mode_from(cfg, KS_MODE_TREE)};
+        ks_reduction_args a{dx.p,      dout.p, rows, cols, axis == -1 ? KS_F32 : KS_BF16, axis == -1 ? KS_F32 : KS_BF16,
+                            axis,      nullptr, 0,    nullptr};
+        size_t need = 0;
+        int s = ks_reduction_workspace_bytes(&c, &a, &need);
+        if (s != KS_OK) return s;
+        if (need > dws.bytes) {
+          if (dws.p) ks_gpu_free(dws.p);
+          dws.p = nullptr;
+          if ((s = dws.alloc(need)) != KS_OK) return s;
+        }
+        a.workspace = dws.p;
+        a.workspace_bytes = dws.bytes;
+        return ks_reduction_launch(&c, &a, st);
+      }
+    }
+    return KS_ERR_OTHER;
+  }
+
+  int output(std::vector<float> *o) override {
+    if (kind == RowKind::kReduction && axis == -1) {
+      float v = 0;
+      int s = ks_gpu_memcpy_dtoh(&v, dout.p, 4, nullptr);
+      if (s == KS_OK) s = ks_gpu_synchronize();
+      o->assign(1, v);
+      return s;
+    }
+    return download_bf16(dout, out_n, o);
+  }
+
+  void reference(std::vector<float> *o) const override {
+    const std::int64_t R = rows, C = cols;
+    o->assign(out_n, 0.f);
+    switch (kind) {
+      case RowKind::kSoftmax:  // refs.py:79-84
+        for (std::int64_t r = 0; r < R; ++r) {
+          const float *xr = &x.f[size_t(r * C)];
+          float mx = -INFINITY;
+          for (std::int64_t c = 0; c < C; ++c) mx = std::max(mx, xr[c]);
+          std::vector<float> e(static_cast<size_t>(C));
+          float s = 0.f;
+          for (std::int64_t c = 0; c < C; ++c) s += (e[size_t(c)] = std::exp(xr[c] - mx));
+          for (std::int64_t c = 0; c < C; ++c) (*o)[size_t(r * C + c)] = rbf(e[size_t(c)] / s);
+        }
+        break;
+      case RowKind::kLayerNorm:  // refs.py:87-99, two-pass biased variance
+        for (std::int64_t r = 0; r < R; ++r) {
+          const float *xr = &x.f[size_t(r * C)];
+          double s = 0;
+          for (std::int64_t c = 0; c < C; ++c) s += xr[c];
+          const float mean = float(s / double(C));
+          double q = 0;
+          for (std::int64_t c = 0; c < C; ++c) q += double(xr[c] - mean) * double(xr[c] - mean);
+          const float var = float(q / double(C));
+          const float inv = 1.f / std::sqrt(var + 1e-5f);
+          for (std::int64_t c = 0; c < C; ++c)
+            (*o)[size_t(r * C + c)] = rbf((xr[c] - mean) * inv * p1.f[size_t(c)] + p2.f[size_t(c)]);
+        }
+        break;
+      case RowKind::kBiasGelu:  // refs.py:59-76 (erf in double, like math.erf)
+        for (std::int64_t i = 0; i < R * C; ++i) {
+          const float t = rbf(x.f[size_t(i)] + p1.f[size_t(i % C)]);
+          float y;
+          if (gelu == KS_GELU_TANH) {
+            const double u = std::sqrt(2.0 / M_PI) * (t + 0.044715 * double(t) * t * t);
+            y = float(0.5 * t * (1.0 + std::tanh(u)));
+          } else {
+            const float e = float(std::erf(double(t) * (1.0 / std::sqrt(2.0))));
+            y = 0.5f * t * (1.f + e);
+          }
+          (*o)[size_t(i)] = rbf(y);
+        }
+        break;
+      case RowKind::kReduction:
+        if (axis == -1) {
+          double s = 0;
+          for (float v : xf32) s += v;
+          (*o)[0] = float(s);
+        } else {  // refs.py:102-110
+          std::vector<float> acc(static_cast<size_t>(C), 0.f);
+          for (std::int64_t r = 0; r < R; ++r)
+            for (std::int64_t c = 0; c < C; ++c) acc[size_t(c)] += x.f[size_t(r * C + c)];
+          for (std::int64_t c = 0; c < C; ++c) (*o)[size_t(c)] = rbf(acc[size_t(c)]);
+        }
+        break;
+    }
+  }
+
+  GateVerdict verdict(const std::vector<float> &got, const std::vector<float> &ref) const override {
+    if (kind == RowKind::kReduction && axis == -1) {
+      GateVerdict v;
+      const double rel = std::fabs(double(got[0]) - ref[0]) / std::max(1e-30, std::fabs(double(ref[0])));
+      v.cosine = v.pcc = 1.0;
+      v.max_rel_err = v.floor_rel_err = v.norm_rel_err = rel;
+      v.pass = rel <= 1e-5;
+      v.criterion = "fp32 sum rel-err <= 1e-5 against an fp64 sum";
+      return v;
+    }
+    return bf16_verdict(got, ref);
+  }
+
+  int corrupt_output(void *st) override { return ks_gpu_memset(dout.p, 0, dout.bytes, st); }
+};
+
+class RowFamily : public Family {
+ public:
+  RowKind kind;
+  const char *nm;
+  int gelu = KS_GELU_ERF;
+  RowFamily(RowKind k, const char *n) : kind(k), nm(n) {}
+  const char *name() const override { return nm; }
+  bool check_shape(const std::vector<std::int64_t> &s, std::string *r) const override {
+    if (kind == RowKind::kReduction && s.size() == 1 && s[0] > 0) return true;  // full fp32 sum
+    return valid_elem_shape(s, r, nm);
+  }
+  static std::pair<std::int64_t, std::int64_t> rc(const std::vector<std::int64_t> &s) {
+    return s.size() == 1 ? std::pair{std::int64_t(1), s[0]} : std::pair{s[0], s[1]};
+  }
+  int axis_of(const std::vector<std::int64_t> &s) const { return kind == RowKind::kReduction && s.size() == 1 ? -1 : 0; }
+
+  std::vector<json> enumerate(bool full, const std::vector<std::int64_t> &s) const override {
+    std::vector<json> v;
+    const std::vector<int> blocks = full ? std::vector<int>{128, 256, 512, 1024} : std::vector<int>{128, 256, 512};
+    const std::vector<int> vecs = full ? std::vector<int>{1, 2, 4, 8} : std::vector<int>{4, 8};
+    std::vector<std::string> modes;
+    if (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm) modes = {"onepass", "twopass", "staged"};
+    if (kind == RowKind::kReduction) modes = {"strided", "tree"};
+    for (int b : blocks)
+      for (int vw : (axis_of(s) == -1 ? std::vector<int>{4} : vecs)) {
+        if (modes.empty()) {
+          v.push_back(db::json::object({{"block", json(b)}, {"vec_width", json(vw)},
+                                        {"gelu", json(gelu == KS_GELU_TANH ? "tanh" : "erf")}}));
+        } else {
+          for (const auto &m : modes)
+            v.push_back(db::json::object({{"block", json(b)}, {"vec_width", json(vw)}, {"mode", json(m)}}));
+        }
+      }
+    return v;
+  }
+  ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
+    const auto [r, c] = rc(s);
+    ElemProblem p{r, c, arch, 2, axis_of(s)};
+    const int block = iget(cfg, "block", 0), vec = iget(cfg, "vec_width", 0);
+    switch (kind) {
+      case RowKind::kSoftmax: return validate_config(SoftmaxConfig{block, vec, ElemMode(mode_from(cfg, -1))}, p);
+      case RowKind::kLayerNorm: return validate_config(LayerNormConfig{block, vec, ElemMode(mode_from(cfg, -1))}, p);
+      case RowKind::kBiasGelu: return validate_config(BiasGeluConfig{block, vec, gelu}, p);
+      case RowKind::kReduction: return validate_config(ReductionConfig{block, vec, ElemMode(mode_from(cfg, -1))}, p);
+    }
+    return {false, "unknown family"};
+  }
+  Resources resources(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    const int block = iget(cfg, "block", 256);
+    const int mode = mode_from(cfg, KS_MODE_ONEPASS);
+    const auto [r, c] = rc(s);
+    (void)r;
+    Resources res{64, 512, block, 0};
+    if (kind == RowKind::kReduction) res.regs_per_thread = 40;
+    if (kind == RowKind::kBiasGelu) res.regs_per_thread = 61;
+    if (mode == KS_MODE_STAGED) {
+      const std::int64_t stride = (c * 2 + 127) / 128 * 128;
+      const int stages = int(std::min<std::int64_t>(8, 65536 / std::max<std::int64_t>(stride, 1)));
+      res.smem_bytes = int(stride * (stages + (kind == RowKind::kLayerNorm ? 2 : 0))) + 512;
+      res.regs_per_thread = 80;
+    } else if (block <= 256 && iget(cfg, "vec_width", 8) == 8 && kind != RowKind::kReduction &&
+               kind != RowKind::kBiasGelu) {
+      res.regs_per_thread = 80;  // the prefetching 8-wide instantiation
+    }
+    return res;
+  }
+  LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    const auto [r, c] = rc(s);
+    LaunchGeometry g;
+    g.block_x = iget(cfg, "block", 256);
+    const Resources res = resources(cfg, s);
+    const auto occ = occupancy::compute_occupancy(get_arch("sm_100a"), res.regs_per_thread, res.smem_bytes,
+                                                  g.block_x, 0);
+    const std::int64_t cap = std::int64_t(std::max(1, occ.blocks_per_sm)) * 148;
+    if (kind == RowKind::kBiasGelu) {
+      const std::int64_t nvec = c / std::max(1, iget(cfg, "vec_width", 8));
+      g.grid_x = int((nvec + g.block_x - 1) / g.block_x);
+      g.grid_y = int((r + 31) / 32);
+    } else {
+      g.grid_x = int(std::min<std::int64_t>(r, cap));
+    }
+    g.smem_bytes = res.smem_bytes;
+    return g;
+  }
+  std::string symbol(const json &cfg) const override {
+    const int block = iget(cfg, "block", 0), vec = iget(cfg, "vec_width", 0);
+    switch (kind) {
+      case RowKind::kSoftmax: return kernel_symbol(SoftmaxConfig{block, vec, ElemMode(mode_from(cfg, 0))});
+      case RowKind::kLayerNorm: return kernel_symbol(LayerNormConfig{block, vec, ElemMode(mode_from(cfg, 0))});
+      case RowKind::kBiasGelu: return kernel_symbol(BiasGeluConfig{block, vec, gelu});
+      case RowKind::kReduction: return kernel_symbol(ReductionConfig{block, vec, ElemMode(mode_from(cfg, 3))});
+    }
+    return "";
+  }
+  std::vector<std::int64_t> gate_shape(const std::vector<std::int64_t> &s) const override {
+    if (s.size() == 1) return {std::min<std::int64_t>(s[0], 1 << 22)};
+    const std::int64_t rows = std::max<std::int64_t>(1, std::min<std::int64_t>(s[0], (1 << 22) / std::max<std::int64_t>(s[1], 1)));
+    return {rows, s[1]};
+  }
+  roofline::KernelFamily rk() const {
+    switch (kind) {
+      case RowKind::kSoftmax: return roofline::KernelFamily::kSoftmax;
+      case RowKind::kLayerNorm: return roofline::KernelFamily::kLayerNorm;
+      case RowKind::kBiasGelu: return roofline::KernelFamily::kFusedBiasGelu;
+      case RowKind::kReduction: return roofline::KernelFamily::kReduction;
+    }
+    return roofline::KernelFamily::kSoftmax;
+  }
+  std::int64_t flops(const std::vector<std::int64_t> &s, const json &) const override {
+    const auto [r, c] = rc(s);
+    return roofline::compute_flops(rk(), roofline::Shape{0, r * c, c, 0, 2});
+  }
+  std::int64_t bytes(const std::vector<std::int64_t> &s) const override {
+    const auto [r, c] = rc(s);
+    if (kind == RowKind::kReduction)
+      return s.size() == 1 ? r * c * 4 + 4 : r * c * 2 + c * 2;
+    return roofline::compute_bytes_moved(rk(), roofline::Shape{0, r * c, c, 0, 2});
+  }
+  std::unique_ptr<Session> make_session(const std::vector<std::int64_t> &s, std::uint64_t seed,
+                                        std::string *err) const override {
+    auto p = std::make_unique<RowSession>();
+    const auto [r, c] = rc(s);
+    const int st = p->init(kind, r, c, gelu, axis_of(s), seed);
+    if (st != KS_OK) {
+      if (err) *err = std::string(nm) + " session: " + ks_status_string(st);
+      return nullptr;
+    }
+    return p;
+  }
+  std::string generate_source(const json &cfg, const std::vector<std::int64_t> &s) const override {
+    const auto [r, c] = rc(s);
+    const int block = iget(cfg, "block", 256), vec = iget(cfg, "vec_width", 8);
+    std::ostringstream o;
+    o << "// reproducer: " << symbol(cfg) << " at " << shape_str(s) << "\n#include <kernscope_b200.h>\n#include <cstdio>\n"
+      << "int main() {\n  const long long rows = " << r << ", cols = " << c << ";\n  void *x, *p1, *p2, *out, *ws = nullptr;\n"
+      << "  ks_gpu_malloc(&x, rows * cols * 4); ks_gpu_malloc(&p1, cols * 2); ks_gpu_malloc(&p2, cols * 2);\n"
+      << "  ks_gpu_malloc(&out, rows * cols * 4); ks_gpu_memset(x, 0, rows * cols * 4, nullptr);\n"
+      << "  ks_gpu_memset(p1, 0, cols * 2, nullptr); ks_gpu_memset(p2, 0, cols * 2, nullptr);\n  int st = 0;\n";
+    switch (kind) {
+      case RowKind::kSoftmax:
+        o << "  ks_softmax_config cfg{" << block << ", " << vec << ", " << mode_from(cfg, 0) << "};\n"
+          << "  ks_softmax_args a{x, out, rows, cols};\n  st = ks_softmax_launch(&cfg, &a, nullptr);\n";
+        break;
+      case RowKind::kLayerNorm:
+        o << "  ks_layernorm_config cfg{" << block << ", " << vec << ", " << mode_from(cfg, 0) << "};\n"
+          << "  ks_layernorm_args a{x, p1, p2, out, rows, cols, 1e-5f};\n  st = ks_layernorm_launch(&cfg, &a, nullptr);\n";
+        break;
+      case RowKind::kBiasGelu:
+        o << "  ks_bias_gelu_config cfg{" << block << ", " << vec << ", " << gelu << "};\n"
+          << "  ks_bias_gelu_args a{x, p1, out, rows * cols, cols};\n  st = ks_bias_gelu_launch(&cfg, &a, nullptr);\n";
+        break;
+      case RowKind::kReduction:
+        o << "  ks_reduction_config cfg{" << block << ", " << vec << ", " << mode_from(cfg, 3) << "};\n"
+          << "  ks_reduction_args a{x, out, rows, cols, " << (axis_of(s) == -1 ? "KS_F32, KS_F32, -1" : "KS_BF16, KS_BF16, 0")
+          << ", nullptr, 0, nullptr};\n  size_t need = 0; ks_reduction_workspace_bytes(&cfg, &a, &need);\n"
+          << "  if (need) { ks_gpu_malloc(&ws, need); a.workspace = ws; a.workspace_bytes = need; }\n"
+          << "  st = ks_reduction_launch(&cfg, &a, nullptr);\n";
+        break;
+    }
+    o << "  if (st == 0) st = ks_gpu_synchronize();\n  std::printf(\"%s\\n\", ks_status_string(st));\n"
+      << "  return st == 0 ? 0 : 1;\n}\n";
+    return o.str();
+  }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// typed API
+// ---------------------------------------------------------------------------
+static ConfigVerdict from_status(int st, const char *reason) {
+  if (st == KS_OK) return {true, ""};
+  return {false, reason[0] ? std::string(reason) : std::string(ks_status_string(st))};
+}
+
+static ConfigVerdict check_arch(const std::string &arch) {
+  if (!has_arch(arch)) return {false, "unknown arch '" + arch + "' (sm_100a DB)"};
+  return {true, ""};
+}
+
+ConfigVerdict validate_config(const MatmulConfig &c, const MatmulProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m};
+  char reason[256] = {0};
+  ConfigVerdict v = from_status(ks_matmul_validate(&k, p.m, p.n, p.k, reason, sizeof(reason)), reason);
+  if (!v.valid) return v;
+  const ArchInfo &arch = get_arch(p.arch);
+  if (smem_bytes(c) > arch.smem_per_block_max_bytes)
+    return {false, "matmul: shared memory " + std::to_string(smem_bytes(c)) + " > " +
+                       std::to_string(arch.smem_per_block_max_bytes) + " bytes per CTA"};
+  if (pow2_cols(c.acc_stages * c.tile_n) > arch.tmem_columns_per_sm)
+    return {false, "matmul: accumulators need more than 512 TMEM columns"};
+  return v;
+}
+
+ConfigVerdict validate_config(const FlashAttentionConfig &c, const FlashAttentionProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_flash_attention_config k{c.tile_m, c.tile_n, c.stages, c.causal ? 1 : 0};
+  ks_flash_attention_args a{nullptr, nullptr, nullptr, nullptr, 1, p.batch_heads, p.nq, p.nk, p.d, 0.f};
+  char reason[256] = {0};
+  return from_status(ks_flash_attention_validate(&k, &a, reason, sizeof(reason)), reason);
+}
+
+ConfigVerdict validate_config(const SoftmaxConfig &c, const ElemProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_softmax_config k{c.block, c.vec_width, int(c.mode)};
+  char reason[256] = {0};
+  return from_status(ks_softmax_validate(&k, p.rows, p.cols, reason, sizeof(reason)), reason);
+}
+
+ConfigVerdict validate_config(const LayerNormConfig &c, const ElemProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_layernorm_config k{c.block, c.vec_width, int(c.mode)};
+  char reason[256] = {0};
+  return from_status(ks_layernorm_validate(&k, p.rows, p.cols, reason, sizeof(reason)), reason);
+}
+
+ConfigVerdict validate_config(const BiasGeluConfig &c, const ElemProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_bias_gelu_config k{c.block, c.vec_width, c.gelu};
+  char reason[256] = {0};
+  return from_status(ks_bias_gelu_validate(&k, p.rows * p.cols, p.cols, reason, sizeof(reason)), reason);
+}
+
+ConfigVerdict validate_config(const ReductionConfig &c, const ElemProblem &p) noexcept {
+  if (auto a = check_arch(p.arch); !a.valid) return a;
+  ks_reduction_config k{c.block, c.vec_width, int(c.mode)};
+  ks_reduction_args a{nullptr, nullptr, p.rows, p.cols, p.axis == -1 ? KS_F32 : KS_BF16,
+                      p.axis == -1 ? KS_F32 : KS_BF16, p.axis, nullptr, 0, nullptr};
+  char reason[256] = {0};
+  return from_status(ks_reduction_validate(&k, &a, reason, sizeof(reason)), reason);
+}
+
+std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
+  // A ring (128 x 64 bf16) + B ring (64 x tile_n bf16) + barriers + 1 KB alignment slack
+  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * c.tile_n * 2) + (2 * c.stages + 2 * c.acc_stages + 1) * 8 +
+         16 + 1024;
+}
+
+std::int64_t smem_bytes(const FlashAttentionConfig &, const FlashAttentionProblem &) noexcept {
+  // Q0, Q1 and a 2-stage K/V ring of 128 x 128 bf16 tiles + barriers + alignment slack
+  return 6 * 32768 + 16 * 8 + 16 + 1024;
+}
+
+LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) noexcept {
+  LaunchGeometry g;
+  const std::int64_t tiles = ((p.m + c.tile_m - 1) / c.tile_m) * ((p.n + c.tile_n - 1) / c.tile_n);
+  g.grid_x = int(std::min<std::int64_t>(tiles, 148));  // persistent: one CTA per SM
+  g.block_x = 192;
+  g.smem_bytes = int(smem_bytes(c));
+  g.tmem_columns = pow2_cols(c.acc_stages * c.tile_n);
+  return g;
+}
+
+LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttentionProblem &p) noexcept {
+  LaunchGeometry g;
+  g.grid_x = int((p.nq + 255) / 256);
+  g.grid_y = int(p.batch_heads);
+  g.block_x = p.d == 128 ? 320 : 128;
+  if (p.d != 128) g.grid_x = int((p.nq + 3) / 4);
+  g.smem_bytes = p.d == 128 ? int(smem_bytes(c, p)) : 4 * 256 * 4;
+  g.tmem_columns = p.d == 128 ? 512 : 0;
+  return g;
+}
+
+static std::string sym(const char *fam, const void *cfg) {
+  char buf[256] = {0};
+  return ks_kernel_symbol(fam, cfg, buf, sizeof(buf)) == KS_OK ? std::string(buf) : std::string();
+}
+std::string kernel_symbol(const MatmulConfig &c) {
+  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m};
+  return sym("matmul", &k);
+}
+std::string kernel_symbol(const FlashAttentionConfig &c) {
+  ks_flash_attention_config k{c.tile_m, c.tile_n, c.stages, c.causal ? 1 : 0};
+  return sym("flash_attention", &k);
+}
+std::string kernel_symbol(const SoftmaxConfig &c) {
+  ks_softmax_config k{c.block, c.vec_width, int(c.mode)};
+  return sym("softmax", &k);
+}
+std::string kernel_symbol(const LayerNormConfig &c) {
+  ks_layernorm_config k{c.block, c.vec_width, int(c.mode)};
+  return sym("layernorm", &k);
+}
+std::string kernel_symbol(const BiasGeluConfig &c) {
+  ks_bias_gelu_config k{c.block, c.vec_width, c.gelu};
+  return sym("bias_gelu", &k);
+}
+std::string kernel_symbol(const ReductionConfig &c) {
+  ks_reduction_config k{c.block, c.vec_width, int(c.mode)};
+  return sym("reduction", &k);
+}
+
+// ---------------------------------------------------------------------------
+// registry
+// ---------------------------------------------------------------------------
+namespace {
+struct Registry {
+  MatmulFamily matmul;
+  FlashFamily flash, flash_causal;
+  RowFamily softmax{RowKind::kSoftmax, "softmax"};
+  RowFamily layernorm{RowKind::kLayerNorm, "layernorm"};
+  RowFamily bias_gelu{RowKind::kBiasGelu, "bias_gelu"};
+  RowFamily bias_gelu_tanh{RowKind::kBiasGelu, "bias_gelu"};
+  RowFamily reduction{RowKind::kReduction, "reduction"};
+  Registry() {
+    flash_causal.causal = true;
+    bias_gelu_tanh.gelu = KS_GELU_TANH;
+  }
+};
+Registry &reg() {
+  static Registry r;
+  return r;
+}
+}  // namespace
+
+const Family *find_family(const std::string &name) {
+  Registry &r = reg();
+  if (name == "matmul") return &r.matmul;
+  if (name == "flash_attention" || name == "attention") return &r.flash;
+  if (name == "flash_attention:causal") return &r.flash_causal;
+  if (name == "softmax") return &r.softmax;
+  if (name == "layernorm") return &r.layernorm;
+  if (name == "bias_gelu") return &r.bias_gelu;
+  if (name == "bias_gelu:tanh") return &r.bias_gelu_tanh;
+  if (name == "reduction") return &r.reduction;
+  return nullptr;
+}
+
+const std::vector<std::string> &family_names() {
+  static const std::vector<std::string> n{"matmul", "bias_gelu", "softmax", "layernorm", "reduction",
+                                          "flash_attention"};
+  return n;
+}
+
+}  // namespace kernscope::tune
