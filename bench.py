@@ -240,51 +240,32 @@ class ClockSampler:
 def _dist_setup(args):
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
+    from kernscope_b200 import dist
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    else:
+    rank, world, local = dist.setup(backend="nccl", timeout_s=120)
+    if world == 1:
         torch.cuda.set_device(0)
     return rank, world, local
 
 
 def _barrier(world):
-    import torch
+    from kernscope_b200 import dist
 
-    torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize()
+    dist.barrier(world)
 
 
 def _max_over_ranks(v, world):
-    import torch
+    from kernscope_b200 import dist
 
-    if world == 1:
-        return v
-    import torch.distributed as dist
-
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return dist.max_over_ranks(v, world, device="cuda")
 
 
 def _combine(w, world):
     """The reduction's cross-GPU combine: all-reduce of the fp64 partial."""
     if world > 1 and w.name == "reduction":
-        import torch.distributed as dist
+        from kernscope_b200 import dist
 
-        dist.all_reduce(w.sets[0][1][1])
+        dist.combine_partials(w.sets[0][1][1], world)
 
 
 def measure_device(w, steps, warmup, world, graph=True):
@@ -300,7 +281,9 @@ def measure_device(w, steps, warmup, world, graph=True):
     torch.cuda.synchronize()
     g = None
     per_graph = w.rotate if w.rotate > 1 else 1
-    if graph and world == 1:
+    # graphs hold only this rank's kernels; the reduction's per-step NCCL
+    # combine stays outside a graph (its launch is ~165 us, host-paced is fine)
+    if graph and (world == 1 or w.name != "reduction"):
         reps = max(1, 8 // per_graph) if per_graph < 8 else 1
         per_graph *= reps
         s = torch.cuda.Stream()
@@ -466,9 +449,24 @@ def run_families(names, args, rank, world):
     return out
 
 
+def _ref_worker_init():
+    # one BLAS thread per process: the pool itself uses every core
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"
+
+
+# Rows (matmul: A rows; attention: query rows; reduction: 64K-element blocks)
+# per worker per step, sized to ~0.1-0.5 s of numpy work on one core.
+REF_CHUNK = {"softmax": 256, "layernorm": 512, "bias_gelu": 64, "reduction": 512, "matmul": 256,
+             "matmul_65536": 256, "flash_attention": 256}
+
+
 def main_reference(args):
-    """--impl reference: the reference's CPU path (the oracle port of
-    refs.py) on the host cores, rank 0 only, bounded samples per step."""
+    """--impl reference: the reference's CPU path (the numpy port of the
+    reference's refs.py) on every host core, rank 0 only.  A step is one
+    bounded sample of the workload: each of the `cores` worker processes
+    computes its own row chunk; the inputs are generated outside the timed
+    part, and the step's time is the slowest worker's compute time."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -477,67 +475,77 @@ def main_reference(args):
     spec = WORKLOADS[args.workload]
     cores = os.cpu_count() or 1
     ctx = mp.get_context("spawn")
-    chunk_rows = 64
-    with ctx.Pool(cores) as pool:
-        def one_step():
-            t0 = time.perf_counter()
-            res = pool.map(_ref_chunk, [(args.workload, i * chunk_rows, chunk_rows) for i in range(cores)])
-            return time.perf_counter() - t0, sum(res)
-        for _ in range(args.warmup):
-            one_step()
+    chunk = REF_CHUNK[args.workload]
+    with ctx.Pool(cores, initializer=_ref_worker_init) as pool:
+        def one_step(step):
+            jobs = [(args.workload, (step * cores + i) * chunk, chunk) for i in range(cores)]
+            res = pool.map(_ref_chunk, jobs)
+            return max(r[1] for r in res), sum(r[0] for r in res)
+        for i in range(args.warmup):
+            one_step(i)
         tt, uu = 0.0, 0.0
-        for _ in range(args.steps):
-            dt, u = one_step()
+        for i in range(args.steps):
+            dt, u = one_step(args.warmup + i)
             tt += dt
             uu += u
     val = uu / tt
     unit = "TFLOP/s" if spec["bound"] == "tensor" else "GB/s"
     line = {"metric": "bf16 TFLOP/s & HBM GB/s per kernel family as % of B200 roofline",
-            "impl": "reference", "value": round(val, 4), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+            "impl": "reference", "value": round(val, 6), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(tt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
             "config": {"workload": spec["desc"], "baseline_config": spec["config"]},
-            "cpu_baseline": {"value": round(val, 4), "unit": unit, "cores": cores, "kind": "port",
-                             "sample": f"{cores} x {chunk_rows}-row chunks per step (numpy restatement of "
-                                       "tests/golden/kernscope_golden/refs.py, one process per core)"},
-            "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cores, "kind": "port",
+                             "sample": f"{cores} worker processes x {chunk}-row chunks per step, compute only "
+                                       "(numpy restatement of tests/golden/kernscope_golden/refs.py, 1 BLAS "
+                                       "thread per process)"},
+            "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
 
 
 def _ref_chunk(job):
+    """(units, seconds) of the reference computation for one row chunk."""
     name, row0, nrows = job
     from oracle import inputs as oin
     from oracle import refs as orf
 
     shape = WORKLOADS[name]["shape"]
+    if name in ("softmax", "layernorm", "bias_gelu"):
+        rows = shape[0]
+        row0 %= rows
+        nrows = min(nrows, rows - row0)
     if name == "softmax":
         x = oin.baseline_inputs("softmax", shape, seed=1, row0=row0, nrows=nrows)["x"]
-        orf.softmax(x)
-        return x.size * 4 / 1e9
+        t0 = time.perf_counter(); orf.softmax(x); dt = time.perf_counter() - t0
+        return x.size * 4 / 1e9, dt
     if name == "layernorm":
         d = oin.baseline_inputs("layernorm", shape, seed=2, row0=row0, nrows=nrows)
-        orf.layernorm(d["x"], d["gamma"], d["beta"])
-        return d["x"].size * 4 / 1e9
+        t0 = time.perf_counter(); orf.layernorm(d["x"], d["gamma"], d["beta"]); dt = time.perf_counter() - t0
+        return d["x"].size * 4 / 1e9, dt
     if name == "bias_gelu":
         d = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=row0, nrows=nrows)
-        orf.bias_gelu_tanh(d["x"], d["bias"])
-        return d["x"].size * 4 / 1e9
+        t0 = time.perf_counter(); orf.bias_gelu_tanh(d["x"], d["bias"]); dt = time.perf_counter() - t0
+        return d["x"].size * 4 / 1e9, dt
     if name == "reduction":
+        (n,) = shape
         cnt = nrows * 65536
-        x = oin.baseline_inputs("reduction_full", shape, seed=2, row0=row0 * 65536, nrows=cnt)["x"]
-        orf.sum_full_f64(x)
-        return cnt * 4 / 1e9
+        i0 = (row0 * 65536) % (n - cnt)
+        x = oin.baseline_inputs("reduction_full", shape, seed=2, row0=i0, nrows=cnt)["x"]
+        t0 = time.perf_counter(); orf.sum_full_f64(x); dt = time.perf_counter() - t0
+        return cnt * 4 / 1e9, dt
     if name.startswith("matmul"):
         m, n, k = shape
-        d = oin.baseline_inputs("matmul", shape, seed=3, row0=row0, nrows=nrows)
-        orf.matmul(d["a"], d["b"])
-        return 2 * nrows * n * k / 1e12
+        r0 = row0 % m
+        d = oin.baseline_inputs("matmul", shape, seed=3, row0=r0, nrows=min(nrows, m - r0))
+        t0 = time.perf_counter(); orf.matmul(d["a"], d["b"]); dt = time.perf_counter() - t0
+        return 2 * d["a"].shape[0] * n * k / 1e12, dt
     b, h, s, dd = shape
-    d = oin.baseline_inputs("attention", (b, h, s, s, dd), seed=4, row0=0, nrows=1)
-    q = d["q"][0, s - nrows:]
-    orf.attention(q, d["k"][0], d["v"][0])
-    return 4 * dd * q.shape[0] * s / 1e12
+    head = (row0 // s) % (b * h)
+    d = oin.baseline_inputs("attention", (b, h, s, s, dd), seed=4, row0=head, nrows=1)
+    q = d["q"][0, s - nrows:]  # the last rows: each attends to (almost) all keys under the causal mask
+    t0 = time.perf_counter(); orf.attention(q, d["k"][0], d["v"][0]); dt = time.perf_counter() - t0
+    return 4 * dd * q.shape[0] * s / 1e12, dt
 
 
 def main():
@@ -596,7 +604,10 @@ def main():
     torch.cuda.empty_cache()
     fams = None
     if not args.no_families:
-        names = [n for n in WORKLOADS if n != args.workload]
+        # the heaviest (power-capped) workload last, so it does not heat the GPU
+        # for the others
+        order = ["layernorm", "bias_gelu", "reduction", "softmax", "flash_attention", "matmul", "matmul_65536"]
+        names = [n for n in order if n != args.workload]
         fams = run_families(names, args, rank, world)
     cpu = None
     if rank == 0 and world == 1:
@@ -627,10 +638,9 @@ def main():
         if fams is not None:
             line["families"] = fams
         print(json.dumps(line))
-    if world > 1:
-        import torch.distributed as dist
+    from kernscope_b200 import dist
 
-        dist.destroy_process_group()
+    dist.teardown(world)
     return 0
 
 

@@ -1,0 +1,93 @@
+"""CPU, world_size 2 gloo ranks: the multi-GPU host logic of the benchmark.
+
+Each rank sums its shard of the full-sum workload in fp64 (the GPU kernel's
+partial), the ranks combine with one all-reduce (the reduction family's only
+collective), and the job time is the maximum over ranks.  Also: a rank that
+raises before the collective makes the other rank's collective fail within
+the process-group timeout instead of hanging (failure on the host, no GPU).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, n, q, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+
+    from kernscope_b200 import dist
+    from oracle import inputs as oin
+
+    r, w, _ = dist.setup(backend="gloo", timeout_s=10)
+    try:
+        if rank == fail_rank:
+            raise RuntimeError("injected rank failure")
+        r0, r1 = dist.shard_rows(n, r, w)
+        x = oin.baseline_inputs("reduction_full", (n,), seed=2, row0=r0, nrows=r1 - r0)["x"]
+        mine = float(np.sum(x, dtype=np.float64))
+        part = torch.tensor([mine], dtype=torch.float64)
+        total = dist.combine_partials(part, w)  # in place: part now holds the job's sum
+        t = dist.max_over_ranks(1.0 + rank, w)
+        q.put((rank, float(total.item()), mine, t, None))
+    except Exception as exc:  # noqa: BLE001 - report to the parent
+        q.put((rank, None, None, None, type(exc).__name__ + ": " + str(exc)[:120]))
+    finally:
+        dist.teardown(w)
+
+
+def _run(world, n, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n, q, fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    return sorted(out)
+
+
+def test_two_rank_sum_combine_and_max_time():
+    n = 3_000_001
+    out = _run(2, n)
+    from oracle import inputs as oin
+
+    ref = float(np.sum(oin.baseline_inputs("reduction_full", (n,), seed=2)["x"], dtype=np.float64))
+    for rank, total, part, t, err in out:
+        assert err is None
+        assert abs(total - ref) <= 1e-5 * ref
+        assert t == 2.0  # max over ranks of 1 + rank
+    assert abs(out[0][2] + out[1][2] - ref) <= 1e-9 * ref
+
+
+def test_shard_rows_cover():
+    from kernscope_b200 import dist
+
+    for rows, world in ((4096, 8), (10, 3), (1, 2)):
+        spans = [dist.shard_rows(rows, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == rows
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+@pytest.mark.timeout(180)
+def test_failed_rank_ends_collective_with_error():
+    out = _run(2, 1000, fail_rank=1)
+    errs = {rank: err for rank, _, _, _, err in out}
+    assert "injected rank failure" in errs[1]
+    assert errs[0] is not None  # the surviving rank's all-reduce errored out instead of hanging
