@@ -7,8 +7,10 @@
 // products.  Same algorithm here (Dao et al. 2022, online softmax), mapped to
 // Blackwell:
 //
-//   * one CTA = one (batch*head, 256-query block) = two 128-row Q tiles;
-//     K/V walked in 128-row tiles through a 2-stage TMA ring;
+//   * config tile_m 256 (fa_fwd_kernel): one CTA = one (batch*head,
+//     256-query block) = two 128-row Q tiles; tile_m 128 (fa_fwd1_kernel,
+//     further below): one Q tile with S double-buffered.  K/V walked in
+//     128-row tiles through a 2-stage TMA ring;
 //   * warp 8 (one lane): TMA producer (Q once, K_j and V_j per tile,
 //     128-byte swizzle, 3-D maps [BH][N][d] so out-of-range rows read zeros);
 //   * warp 9 (one lane): tcgen05.mma issuer.  TMEM columns: S0 [0,128),
@@ -416,6 +418,305 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// One 128-row Q tile per CTA with S double-buffered in TMEM.
+//
+// TMEM: S[0] columns [0,128), S[1] [128,256), O [256,384).  Because S(j+2)
+// reuses the region of S(j) rather than the one being read, the tensor core
+// computes S(j+1) while the softmax works on S(j): the MMA issue order is
+// S(0), S(1), then per K/V tile j: O += P(j) V(j), S(j+2).  The two softmax
+// warpgroups split each S tile by columns (keys [0,64) and [64,128)): both
+// hold all 128 rows, exchange their partial row maxima through shared
+// memory once per tile, keep partial row sums, and write their half of P
+// (packed bf16) over the S columns they have read: keys [0,64) into columns
+// [0,32), keys [64,128) into [64,96).  Each warpgroup rescales its half of
+// O (64 of the 128 head-dim columns) when the running max grows by more than
+// 2^8, after the previous P V has completed.  The pipeline period is the
+// longer of the softmax time and one tile's two MMAs (S and P V).
+// ---------------------------------------------------------------------------
+struct Fa1Layout {
+  static constexpr uint32_t q_off = 0;
+  static constexpr uint32_t k_off = q_off + kTileBytes;
+  static constexpr uint32_t v_off = k_off + kStages * kTileBytes;
+  static constexpr uint32_t red_off = v_off + kStages * kTileBytes;  // float [2 steps][2 WGs][128 rows]
+  static constexpr uint32_t lsum_off = red_off + 2 * 2 * 128 * 4;    // float [2 WGs][128 rows]
+  static constexpr uint32_t bar_off = lsum_off + 2 * 128 * 4;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, pv_done, o_full, red, drain
+  static constexpr uint32_t n_bars = 1 + 4 * kStages + 2 + 5;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
+  static constexpr uint32_t bytes = misc_off + 16;
+  static constexpr uint32_t smem_request = bytes + 1024;
+};
+
+// O += P V for the split P layout above.
+KS_DEV void issue_pv_split(uint32_t o_tmem, uint32_t s_tmem, uint32_t v_addr, bool accumulate) {
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, true);
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk)
+    ks_umma_ts(o_tmem, s_tmem + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8),
+               ks_umma_desc_sw128(v_addr + kk * 2048, kBox, 1024), idesc, accumulate || kk > 0);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd1_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
+                   float scale_log2, int causal, KsWait wait) {
+  using L = Fa1Layout;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ks_smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off);
+  uint64_t *q_full = bars;
+  uint64_t *k_full = bars + 1;
+  uint64_t *k_empty = k_full + kStages;
+  uint64_t *v_full = k_empty + kStages;
+  uint64_t *v_empty = v_full + kStages;
+  uint64_t *s_full = v_empty + kStages;
+  uint64_t *p_full = s_full + 2;
+  uint64_t *pv_done = p_full + 1;
+  uint64_t *o_full = pv_done + 1;
+  uint64_t *red_bar = o_full + 1;
+  uint64_t *drain = red_bar + 1;
+  float *red = reinterpret_cast<float *>(smem + L::red_off);
+  float *lsum = reinterpret_cast<float *>(smem + L::lsum_off);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qb = (nq + kTile - 1) / kTile;
+  const int qb = num_qb - 1 - int(blockIdx.x);  // heaviest causal blocks first
+  const int bh = blockIdx.y;
+  const int q0 = qb * kTile;
+  int n_kv = (nk + kTile - 1) / kTile;
+  if (causal) n_kv = min(n_kv, (min(q0 + kTile, nq) - 1) / kTile + 1);
+
+  if (threadIdx.x == 0) {
+    ks_mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      ks_mbar_init(k_full + s, 1);
+      ks_mbar_init(k_empty + s, 1);
+      ks_mbar_init(v_full + s, 1);
+      ks_mbar_init(v_empty + s, 1);
+    }
+    ks_mbar_init(s_full + 0, 1);
+    ks_mbar_init(s_full + 1, 1);
+    ks_mbar_init(p_full, 8);
+    ks_mbar_init(pv_done, 1);
+    ks_mbar_init(o_full, 1);
+    ks_mbar_init(red_bar, 8);
+    ks_mbar_init(drain, 1);
+    *abort = 0;
+    ks_fence_mbar_init();
+    ks_prefetch_tmap(&tm_q);
+    ks_prefetch_tmap(&tm_k);
+    ks_prefetch_tmap(&tm_v);
+  }
+  if (warp == 9) {
+    ks_tmem_alloc(tmem_slot, 512);
+    ks_tmem_relinquish();
+  }
+  ks_tc_fence_before();
+  __syncthreads();
+  ks_tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      ks_mbar_arrive_expect_tx(q_full, kTileBytes);
+      for (int h = 0; h < 2; ++h) ks_tma_load_3d(smem + L::q_off + h * kBox, &tm_q, q_full, h * 64, q0, bh);
+      uint32_t k_armed = 0, k_par = 0, v_armed = 0, v_par = 0;
+      auto load = [&](const CUtensorMap *m, uint64_t *full, uint64_t *empty, uint32_t off, int j, uint32_t &armed,
+                      uint32_t &par) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!ks_mbar_wait(empty + st, ph ^ 1u, abort, wait)) return false;
+        uint8_t *dst = smem + off + st * kTileBytes;
+        ks_mbar_arrive_expect_tx(full + st, kTileBytes);
+        for (int h = 0; h < 2; ++h) ks_tma_load_3d(dst + h * kBox, m, full + st, h * 64, j * kTile, bh);
+        armed |= 1u << st;
+        par = (par & ~(1u << st)) | (ph << st);
+        return true;
+      };
+      bool ok = load(&tm_k, k_full, k_empty, L::k_off, 0, k_armed, k_par);
+      if (ok && n_kv > 1) ok = load(&tm_k, k_full, k_empty, L::k_off, 1, k_armed, k_par);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        ok = load(&tm_v, v_full, v_empty, L::v_off, j, v_armed, v_par);
+        if (ok && j + 2 < n_kv) ok = load(&tm_k, k_full, k_empty, L::k_off, j + 2, k_armed, k_par);
+      }
+      // teardown: the loads issued above have landed
+      ks_mbar_wait(q_full, 0, nullptr, wait);
+      for (int s = 0; s < kStages; ++s) {
+        if (k_armed & (1u << s)) ks_mbar_wait(k_full + s, (k_par >> s) & 1u, nullptr, wait);
+        if (v_armed & (1u << s)) ks_mbar_wait(v_full + s, (v_par >> s) & 1u, nullptr, wait);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      const uint32_t q_addr = ks_smem_u32(smem + L::q_off);
+      const uint32_t k_addr = ks_smem_u32(smem + L::k_off);
+      const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
+      const uint32_t t_o = tmem + 256;
+      auto s_mma = [&](int j) {
+        const int st = j % kStages;
+        if (!ks_mbar_wait(k_full + st, (j / kStages) & 1, abort, wait)) return false;
+        ks_tc_fence_after();
+        issue_s(tmem + (j & 1) * 128, q_addr, k_addr + st * kTileBytes);
+        ks_umma_commit(k_empty + st);
+        ks_umma_commit(s_full + (j & 1));
+        return true;
+      };
+      bool ok = ks_mbar_wait(q_full, 0, abort, wait) && s_mma(0);
+      if (ok && n_kv > 1) ok = s_mma(1);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kStages;
+        if (!ks_mbar_wait(v_full + st, (j / kStages) & 1, abort, wait)) break;
+        if (!ks_mbar_wait(p_full, j & 1, abort, wait)) break;
+        ks_tc_fence_after();
+        issue_pv_split(t_o, tmem + (j & 1) * 128, v_addr + st * kTileBytes, j > 0);
+        ks_umma_commit(pv_done);
+        ks_umma_commit(v_empty + st);
+        if (j + 1 == n_kv) ks_umma_commit(o_full);
+        if (j + 2 < n_kv && !s_mma(j + 2)) break;
+      }
+      ks_umma_commit(drain);
+      ks_mbar_wait(drain, 0, nullptr, wait);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int wg = warp >> 2;        // column half of each S tile: keys [64 wg, 64 wg + 64)
+    const int qd = warp & 3;         // TMEM lane quadrant
+    const int row = qd * 32 + lane;  // row within the tile = TMEM lane
+    const int qrow = q0 + row;
+    const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t my_col = 64 * wg;
+    const uint32_t o_col = 256 + 64 * wg;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const uint32_t s_col = (j & 1) * 128 + my_col;
+      if (!ks_mbar_wait(s_full + (j & 1), (j >> 1) & 1, abort, wait)) {
+        ok = false;
+        break;
+      }
+      ks_tc_fence_after();
+      uint32_t r[64];
+      ks_tmem_ld32_at<0>(lane_addr + s_col, r);
+      ks_tmem_ld32_at<32>(lane_addr + s_col + 32, r);
+      ks_tmem_wait_ld();
+      const int key0 = j * kTile + int(my_col);
+      int lim = nk - key0;  // valid keys among this warpgroup's 64
+      if (causal) lim = min(lim, qrow - key0 + 1);
+      if (!__all_sync(0xffffffffu, lim >= 64)) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c >= lim) r[c] = 0xff800000u;  // -inf
+      }
+      float mm[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        mm[u] = max3(__uint_as_float(r[u]), __uint_as_float(r[u + 4]), __uint_as_float(r[u + 8]));
+#pragma unroll
+      for (int c = 12; c < 60; c += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mm[u] = max3(mm[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 4 + u]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mm[u] = fmaxf(mm[u], __uint_as_float(r[60 + u]));
+      const float pm = fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3]));
+      // exchange the partial maxima with the other warpgroup (bounded wait)
+      red[((j & 1) * 2 + wg) * 128 + row] = pm;
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(red_bar);
+      if (!ks_mbar_wait(red_bar, j & 1, abort, wait)) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(pm, red[((j & 1) * 2 + (wg ^ 1)) * 128 + row]);
+      const float m_new = fmaxf(m, mx * scale_log2);
+      const bool grow = m_new > m + 8.f;  // also true on the first finite max
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O must hold every earlier P V before it is rescaled
+        if (!ks_mbar_wait(pv_done, (j - 1) & 1, abort, wait)) {
+          ok = false;
+          break;
+        }
+        ks_tc_fence_after();
+        const float alpha = grow ? ex2(m - m_new) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+          ks_tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(lane_addr + o_col + c * 32, o);
+        }
+        ks_tmem_wait_st();
+      }
+      if (grow) {
+        l *= ex2(m - m_new);
+        m = m_new;
+      }
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+      const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
+      uint32_t p[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const F2 x = fma2(F2{__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])}, sc2, nm2);
+        const F2 e{ex2(x.x), ex2(x.y)};
+        rsum[c & 3] = add2(rsum[c & 3], e);
+        p[c] = ks_pack_bf16x2(e.x, e.y);
+      }
+      ks_tmem_st32_at<0>(lane_addr + s_col, p);
+      const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
+      l += rs2.x + rs2.y;
+      ks_tmem_wait_st();
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(p_full);
+    }
+    // epilogue: row sum = both warpgroups' partial sums; O / l -> bf16
+    if (ok) {
+      lsum[wg * 128 + row] = l;
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(red_bar);
+      ok = ks_mbar_wait(red_bar, n_kv & 1, abort, wait) && ks_mbar_wait(o_full, 0, abort, wait);
+    }
+    if (ok) {
+      ks_tc_fence_after();
+      const float lt = l + lsum[(wg ^ 1) * 128 + row];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      uint16_t *dst = out + (int64_t(bh) * nq + qrow) * kD + my_col;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+        ks_tmem_wait_ld();
+        if (qrow < nq) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+            w.y = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+            w.z = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+            w.w = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+            *reinterpret_cast<uint4 *>(dst + c * 32 + v * 8) = w;
+          }
+        }
+      }
+    }
+  }
+
+  ks_tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ks_tc_fence_after();
+    ks_tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CUDA-core path for head dims other than 128 (d <= 256; the reference's gate
 // shapes use d = 16 and 32): one warp per query row, keys in chunks of 32
 // (one key per lane for the scores), online softmax with warp shuffles, each
@@ -487,8 +788,10 @@ extern "C" {
 int ks_flash_attention_validate(const ks_flash_attention_config *cfg, const ks_flash_attention_args *a,
                                 char *reason, size_t len) {
   if (!cfg || !a) return KS_ERR_INVALID_ARGS;
-  if (cfg->tile_m != 128 || cfg->tile_n != 128) {
-    ks::set_reason(reason, len, "flash_attention: tile_m and tile_n must be 128 (UMMA M=128 tiles, sm_100a space)");
+  if ((cfg->tile_m != 128 && cfg->tile_m != 256) || cfg->tile_n != 128) {
+    ks::set_reason(reason, len,
+                   "flash_attention: tile_m must be 128 or 256 (query rows per CTA: one or two UMMA M=128 "
+                   "tiles) and tile_n 128");
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->stages != 2) {
@@ -544,11 +847,22 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
     s = ks::encode_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->v, kD, uint64_t(a->nk), bh, rs,
                            rs * uint64_t(a->nk), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != KS_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cfg->tile_m == 128) {
+    cudaError_t e = cudaFuncSetAttribute(fa_fwd1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(Fa1Layout::smem_request));
+    if (e != cudaSuccess) return ks::map_cuda(e);
+    dim3 grid(unsigned((a->nq + kTile - 1) / kTile), unsigned(bh));
+    fa_fwd1_kernel<<<grid, kThreads, Fa1Layout::smem_request, st>>>(
+        tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), scale_log2, cfg->causal,
+        ks::wait_ctx());
+    return ks::map_cuda(cudaGetLastError());
+  }
   cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(FaLayout::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
   dim3 grid(unsigned((a->nq + 2 * kTile - 1) / (2 * kTile)), unsigned(bh));
-  fa_fwd_kernel<<<grid, kThreads, FaLayout::smem_request, static_cast<cudaStream_t>(stream)>>>(
+  fa_fwd_kernel<<<grid, kThreads, FaLayout::smem_request, st>>>(
       tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), scale_log2, cfg->causal,
       ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());

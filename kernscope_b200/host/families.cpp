@@ -350,7 +350,7 @@ class FlashSession : public Session {
     return st;
   }
   int launch(const json &cfg, void *st) override {
-    ks_flash_attention_config c{iget(cfg, "tile_m", 128), iget(cfg, "tile_n", 128), iget(cfg, "stages", 2),
+    ks_flash_attention_config c{iget(cfg, "tile_m", 256), iget(cfg, "tile_n", 128), iget(cfg, "stages", 2),
                                 causal ? 1 : 0};
     ks_flash_attention_args a{dq.p, dk.p, dv.p, dout.p, 1, sh.bh, sh.nq, sh.nk, sh.d, 0.f};
     return ks_flash_attention_launch(&c, &a, st);
@@ -446,10 +446,15 @@ class FlashFamily : public Family {
     return true;
   }
   std::vector<json> enumerate(bool, const std::vector<std::int64_t> &) const override {
-    // TMEM holds exactly two 128x128 S tiles and two 128x128 O tiles (512
-    // columns): the sm_100a space is the 128x128 tile with a 2-stage ring.
-    return {db::json::object({{"tile_m", json(128)}, {"tile_n", json(128)}, {"stages", json(2)},
-                              {"causal", json(causal)}})};
+    // TMEM (512 columns) holds two 128x128 S tiles and two 128x128 O tiles
+    // (tile_m 256: two query tiles per CTA) or two S tiles and one O tile
+    // (tile_m 128: one query tile, S double-buffered); 128-key K/V tiles in a
+    // 2-stage ring.
+    std::vector<json> out;
+    for (int tm : {256, 128})
+      out.push_back(db::json::object({{"tile_m", json(tm)}, {"tile_n", json(128)}, {"stages", json(2)},
+                                      {"causal", json(causal)}}));
+    return out;
   }
   ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
     const FaShape f = fa_shape(s);
@@ -457,18 +462,19 @@ class FlashFamily : public Family {
                            cfg.find("causal") && cfg.find("causal")->as_bool()};
     return validate_config(c, FlashAttentionProblem{f.nq, f.nk, f.d, f.bh, causal, arch, 2});
   }
-  Resources resources(const json &, const std::vector<std::int64_t> &s) const override {
+  static FlashAttentionConfig typed(const json &cfg, bool causal) {
+    return FlashAttentionConfig{iget(cfg, "tile_m", 256), iget(cfg, "tile_n", 128), iget(cfg, "stages", 2), causal};
+  }
+  Resources resources(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
     if (f.d != 128) return Resources{48, 4 * 256 * 4, 128, 0};
-    return Resources{168, int(smem_bytes(FlashAttentionConfig{}, FlashAttentionProblem{})), 320, 512};
+    return Resources{168, int(smem_bytes(typed(cfg, causal), FlashAttentionProblem{})), 320, 512};
   }
   LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
-    return launch_geometry(FlashAttentionConfig{128, 128, 2, causal},
-                           FlashAttentionProblem{f.nq, f.nk, f.d, f.bh, causal, "sm_100a", 2});
-    (void)cfg;
+    return launch_geometry(typed(cfg, causal), FlashAttentionProblem{f.nq, f.nk, f.d, f.bh, causal, "sm_100a", 2});
   }
-  std::string symbol(const json &) const override { return kernel_symbol(FlashAttentionConfig{128, 128, 2, causal}); }
+  std::string symbol(const json &cfg) const override { return kernel_symbol(typed(cfg, causal)); }
   std::vector<std::int64_t> gate_shape(const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
     return {1, 2, std::min<std::int64_t>(std::max(f.nq, f.nk), 256), f.d};
@@ -931,8 +937,11 @@ std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
          16 + 1024;
 }
 
-std::int64_t smem_bytes(const FlashAttentionConfig &, const FlashAttentionProblem &) noexcept {
-  // Q0, Q1 and a 2-stage K/V ring of 128 x 128 bf16 tiles + barriers + alignment slack
+std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProblem &) noexcept {
+  // tile_m 256: Q0, Q1 and a 2-stage K/V ring of 128 x 128 bf16 tiles;
+  // tile_m 128: one Q tile, the K/V ring and the row-statistics exchange
+  // (3 KB); plus barriers and alignment slack
+  if (c.tile_m == 128) return 5 * 32768 + 3072 + 16 * 8 + 16 + 1024;
   return 6 * 32768 + 16 * 8 + 16 + 1024;
 }
 
@@ -948,7 +957,7 @@ LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) no
 
 LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttentionProblem &p) noexcept {
   LaunchGeometry g;
-  g.grid_x = int((p.nq + 255) / 256);
+  g.grid_x = int((p.nq + c.tile_m - 1) / c.tile_m);
   g.grid_y = int(p.batch_heads);
   g.block_x = p.d == 128 ? 320 : 128;
   if (p.d != 128) g.grid_x = int((p.nq + 3) / 4);

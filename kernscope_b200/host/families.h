@@ -47,7 +47,7 @@ struct MatmulProblem {
   int dtype_bytes = 2;
 };
 struct FlashAttentionConfig {
-  int tile_m = 128, tile_n = 128, stages = 2;
+  int tile_m = 256, tile_n = 128, stages = 2;
   bool causal = false;
 };
 struct FlashAttentionProblem {

@@ -68,7 +68,7 @@ def default_matmul_config(m: int, n: int, k: int) -> N.MatmulConfig:
 
 
 def default_flash_attention_config(causal: bool) -> N.FlashAttentionConfig:
-    return N.FlashAttentionConfig(128, 128, 2, 1 if causal else 0)
+    return N.FlashAttentionConfig(256, 128, 2, 1 if causal else 0)
 
 
 def softmax(x: torch.Tensor, out=None, cfg=None, stream=None) -> torch.Tensor:

@@ -64,29 +64,35 @@ def _mh(shape, seed, scale=1.0):
     return mk(nq), mk(nk), mk(nk)
 
 
+@pytest.mark.parametrize("tile_m", [256, 128])
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("shape", [(1, 1, 256, 256, 128), (2, 3, 384, 384, 128), (1, 2, 300, 300, 128),
-                                   (1, 1, 1, 1, 128), (1, 1, 129, 129, 128)])
-def test_attention_multihead(ks, shape, causal):
-    _, ops = ks
+                                   (1, 1, 1, 1, 128), (1, 1, 129, 129, 128), (1, 1, 640, 640, 128)])
+def test_attention_multihead(ks, shape, causal, tile_m):
+    N, ops = ks
     q, k, v = _mh(shape, 7)
-    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal))
+    cfg = N.FlashAttentionConfig(tile_m, 128, 2, int(causal))
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
     _check_mh(o, q, k, v, causal)
 
 
+@pytest.mark.parametrize("tile_m", [256, 128])
 @pytest.mark.parametrize("shape", [(1, 2, 200, 520, 128), (1, 1, 520, 200, 128), (2, 1, 64, 1000, 64)])
-def test_attention_cross_lengths(ks, shape):
-    _, ops = ks
+def test_attention_cross_lengths(ks, shape, tile_m):
+    N, ops = ks
     q, k, v = _mh(shape, 8)
-    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=False))
+    cfg = N.FlashAttentionConfig(tile_m, 128, 2, 0)
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=False, cfg=cfg))
     _check_mh(o, q, k, v, False)
 
 
-def test_attention_large_logits(ks):
+@pytest.mark.parametrize("tile_m", [256, 128])
+def test_attention_large_logits(ks, tile_m):
     """Scores spread far apart force the running-max rescale of O."""
-    _, ops = ks
+    N, ops = ks
     q, k, v = _mh((1, 2, 512, 512, 128), 9, scale=4.0)
-    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=True))
+    cfg = N.FlashAttentionConfig(tile_m, 128, 2, 1)
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=True, cfg=cfg))
     _check_mh(o, q, k, v, True)
 
 
@@ -112,3 +118,5 @@ def test_attention_invalid(ks):
     a.d = 128
     assert N.validate("flash_attention", N.FlashAttentionConfig(64, 128, 2, 1), a)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("flash_attention", N.FlashAttentionConfig(128, 128, 2, 1), a)[0] == 0
+    assert N.validate("flash_attention", N.FlashAttentionConfig(256, 128, 2, 1), a)[0] == 0
+    assert N.validate("flash_attention", N.FlashAttentionConfig(192, 128, 2, 1), a)[0] == N.KS_ERR_INVALID_CONFIG

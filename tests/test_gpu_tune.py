@@ -28,7 +28,8 @@ def tune(cuda_ok):
 def _best_checks(ev):
     measured = [v for v in ev["variants"] if "timings" in v]
     assert measured
-    best = min(measured, key=lambda v: (v["timings"]["median_ms"], v["timings"]["p20_ms"]))
+    # the driver's order: median, then p20, then p80, then enumeration index
+    best = min(measured, key=lambda v: (v["timings"]["median_ms"], v["timings"]["p20_ms"], v["timings"]["p80_ms"]))
     assert ev["best"]["config"] == best["config"]
     assert [v for v in ev["variants"] if v["best"]][0]["config"] == best["config"]
     return best
