@@ -200,6 +200,97 @@ KS_DEV void ks_umma_commit(uint64_t *bar) {
                : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// CTA pairs (clusters of 2, tcgen05 cta_group::2): one MMA issued by the
+// even CTA computes a 256-row tile, each CTA holding 128 rows of A, half of
+// the B columns and 128 lanes of the accumulator.  No multicast: every TMA
+// load writes only the issuing CTA's shared memory; only its completion
+// signal may go to the even CTA's barrier.
+// ---------------------------------------------------------------------------
+KS_DEV uint32_t ks_cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+KS_DEV uint32_t ks_mapa(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// All threads of all CTAs of the cluster (release / acquire at cluster scope).
+KS_DEV void ks_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of any CTA of the cluster (address from ks_mapa).
+KS_DEV void ks_mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+KS_DEV bool ks_mbar_try_wait_acq_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// ks_mbar_wait for a barrier that receives arrivals from the other CTA.
+KS_DEV bool ks_mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort, const KsWait &w) {
+  const uint32_t a = ks_smem_u32(bar);
+  if (ks_mbar_try_wait_acq_cluster(a, parity)) return true;
+  const uint64_t t0 = ks_globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (ks_mbar_try_wait_acq_cluster(a, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (ks_globaltimer() - t0 > w.limit_ns) {
+      ks_record_error(w.err, KS_DEVERR_WAIT_TIMEOUT);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+// TMA load into this CTA's shared memory whose completion (bytes) is counted
+// on a barrier that may belong to the other CTA of the pair.
+KS_DEV void ks_tma_load_2d_pair(void *dst, const CUtensorMap *m, uint32_t bar_cluster_addr, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(ks_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+// TMEM allocation shared by the pair: the same warp of both CTAs executes it.
+KS_DEV void ks_tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ks_smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+KS_DEV void ks_tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+KS_DEV void ks_tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMA (issued by the even CTA only): D[256 x N] (+)= A[256 x K] B[K x N].
+KS_DEV void ks_umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the barrier at `cluster_addr` (either CTA of the pair) when
+// every pair MMA issued so far by this thread has completed.
+KS_DEV void ks_umma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
 KS_DEV void ks_tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 KS_DEV void ks_tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

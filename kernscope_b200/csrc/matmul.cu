@@ -21,6 +21,7 @@
 // Every mbarrier wait is bounded (KsWait): on timeout the kernel records the
 // error word, waits (bounded) for its own TMA loads and MMAs, frees TMEM and
 // returns.  No multicast loads anywhere.
+#include <atomic>
 #include <cmath>
 
 #include "ks_common.cuh"
@@ -229,6 +230,229 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Pair kernel (config tile_m 256): clusters of two CTAs on two SMs compute
+// 256 x BN output tiles with tcgen05 cta_group::2 MMAs (M=256).  Each CTA
+// loads its own 128 rows of A and half (BN/2 columns) of B per K-block, so an
+// SM streams 16 KB of A and BN/2 * 128 bytes of B per 128 x BN x 64 step
+// instead of 16 KB + BN * 128 bytes: B traffic from L2 halves.
+//
+//   * warp 0 (both CTAs): TMA producer for its own shared memory; the
+//     completion bytes of both CTAs' loads count on the even CTA's `full`
+//     barrier (the even producer expects both halves);
+//   * warp 1 (even CTA): issues the pair MMAs; each stage's commit arrives
+//     on `empty` in both CTAs, each tile's on `tfull` in both CTAs;
+//   * warps 2-5 (both CTAs): epilogue of the CTA's 128 accumulator lanes (its
+//     128 rows of the tile, all BN columns), then arrive on the even CTA's
+//     `tempty` (8 warps per tile).
+//
+// All waits are bounded.  Both CTAs stay resident until the pair is done
+// (cluster barriers at start and end): the even CTA's MMAs read the odd
+// CTA's shared memory and write its TMEM.  No load uses multicast.
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES, int ACC>
+struct Mm2Layout {
+  static constexpr uint32_t b_bytes = kBK * (BN / 2) * 2;  // this CTA's half of a B stage
+  static constexpr uint32_t a_off = 0;
+  static constexpr uint32_t b_off = a_off + STAGES * kABytes;
+  static constexpr uint32_t bar_off = b_off + STAGES * b_bytes;
+  // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
+  static constexpr uint32_t n_bars = 2 * STAGES + 2 * ACC + 1;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
+  static constexpr uint32_t bytes = misc_off + 16;
+  static constexpr uint32_t smem_request = bytes + 1024;
+  static constexpr uint32_t tmem_cols_raw = ACC * BN;
+  static constexpr uint32_t tmem_cols = tmem_cols_raw <= 32 ? 32 : tmem_cols_raw <= 64 ? 64
+                                        : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
+};
+
+template <int BN, int STAGES, int ACC>
+__global__ void __launch_bounds__(kThreads, 1)
+    matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                      uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
+  using L = Mm2Layout<BN, STAGES, ACC>;
+  constexpr int kPM = 2 * kBM;  // rows per pair tile
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ks_smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + ACC;
+  uint64_t *drain = bars + 2 * STAGES + 2 * ACC;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ks_cluster_ctarank();  // 0: issues the MMAs
+  const int pair = int(blockIdx.x >> 1), num_pairs = int(gridDim.x >> 1);
+  const int num_m = (M + kPM - 1) / kPM, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ks_mbar_init(full + s, 1);
+      ks_mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < ACC; ++a) {
+      ks_mbar_init(tfull + a, 1);
+      ks_mbar_init(tempty + a, 8);
+    }
+    ks_mbar_init(drain, 1);
+    *abort = 0;
+    ks_fence_mbar_init();
+    ks_prefetch_tmap(&tma_a);
+    ks_prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) {
+    ks_tmem_alloc_pair(tmem_slot, L::tmem_cols);
+    ks_tmem_relinquish_pair();
+  }
+  ks_tc_fence_before();
+  ks_cluster_sync();  // both CTAs' barriers are initialised before any remote signal
+  ks_tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    const uint32_t full_even = ks_mapa(ks_smem_u32(full), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0, armed_parity = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!ks_mbar_wait_cluster(empty + stage, phase ^ 1u, abort, wait)) {
+          ok = false;
+          break;
+        }
+        if (rank == 0) ks_mbar_arrive_expect_tx(full + stage, 2 * (kABytes + L::b_bytes));
+        const uint32_t bar = full_even + stage * 8;
+        uint8_t *a_dst = smem + L::a_off + stage * kABytes;
+        uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
+        ks_tma_load_2d_pair(a_dst, &tma_a, bar, kb * kBK, tm * kPM + int(rank) * kBM);
+#pragma unroll
+        for (int j = 0; j < BN / 128; ++j)
+          ks_tma_load_2d_pair(b_dst + j * kBBoxBytes, &tma_b, bar, tn * BN + int(rank) * (BN / 2) + j * 64,
+                              kb * kBK);
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // teardown: every load issued here has landed (the even CTA's `full`
+    // counts both CTAs' loads; a stage released on `empty` was consumed)
+    for (int s = 0; s < STAGES; ++s)
+      if (armed & (1u << s)) {
+        if (rank == 0)
+          ks_mbar_wait_cluster(full + s, (armed_parity >> s) & 1u, nullptr, wait);
+        else
+          ks_mbar_wait_cluster(empty + s, (armed_parity >> s) & 1u, nullptr, wait);
+      }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = ks_idesc_bf16_f32(kPM, BN, false, true);
+    const uint32_t empty_mine = ks_smem_u32(empty), empty_odd = ks_mapa(empty_mine, 1);
+    const uint32_t tfull_mine = ks_smem_u32(tfull), tfull_odd = ks_mapa(tfull_mine, 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int i = 0;
+    for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+      const int acc = i % ACC;
+      const uint32_t acc_phase = (i / ACC) & 1;
+      if (!ks_mbar_wait_cluster(tempty + acc, acc_phase ^ 1u, abort, wait)) break;
+      ks_tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!ks_mbar_wait_cluster(full + stage, phase, abort, wait)) {
+          ok = false;
+          break;
+        }
+        ks_tc_fence_after();
+        const uint32_t a_addr = ks_smem_u32(smem + L::a_off + stage * kABytes);
+        const uint32_t b_addr = ks_smem_u32(smem + L::b_off + stage * L::b_bytes);
+#pragma unroll
+        for (int k = 0; k < kBK / kUmmaK; ++k) {
+          // same descriptors as the single-CTA kernel; the hardware reads the
+          // odd CTA's A rows and B columns at the same offsets
+          const uint64_t adesc = ks_umma_desc_sw128(a_addr + k * 32, 16, 1024);
+          const uint64_t bdesc = ks_umma_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
+          ks_umma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
+        }
+        ks_umma_commit_pair(empty_mine + stage * 8);
+        ks_umma_commit_pair(empty_odd + stage * 8);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) {
+        ks_umma_commit_pair(tfull_mine + acc * 8);
+        ks_umma_commit_pair(tfull_odd + acc * 8);
+      }
+    }
+    // teardown: all pair MMAs issued here complete before TMEM is freed
+    ks_umma_commit_pair(ks_smem_u32(drain));
+    ks_mbar_wait(drain, 0, nullptr, wait);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t tempty_even = ks_mapa(ks_smem_u32(tempty), 0);
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = int(rank) * kBM + q * 32 + lane;
+    int i = 0;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+      const int acc = i % ACC;
+      const uint32_t acc_phase = (i / ACC) & 1;
+      if (!ks_mbar_wait_cluster(tfull + acc, acc_phase, abort, wait)) break;
+      ks_tc_fence_after();
+      int tm, tn;
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      const int64_t row = int64_t(tm) * kPM + row_in_tile;
+      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        ks_tmem_ld32(t_addr + cc * 32, r);
+        ks_tmem_wait_ld();
+        const int col0 = tn * BN + cc * 32;
+        if (row < M && num_kb > 0) {
+          uint16_t *dst = c + row * N + col0;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (col0 + v * 8 < N) {
+              uint4 w;
+              w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+              w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+              w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+              w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+              *reinterpret_cast<uint4 *>(dst + v * 8) = w;
+            }
+          }
+        }
+      }
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive_cluster(tempty_even + acc * 8);
+    }
+  }
+
+  ks_tc_fence_before();
+  __syncwarp();
+  ks_cluster_sync();  // the pair's MMAs, loads and remote arrivals are done
+  if (warp == 1) {
+    ks_tc_fence_after();
+    ks_tmem_dealloc_pair(tmem_base, L::tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CUDA-core path for shapes the TMA path cannot take (K or N not a multiple
 // of 8, or operands not 16-byte aligned): 64x64 output tile per CTA,
 // 16 x 16 threads with a 4 x 4 register fragment, fp32 accumulate.
@@ -302,6 +526,64 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   return ks::map_cuda(cudaGetLastError());
 }
 
+// Pair kernel launch: clusters of 2 via cudaLaunchKernelEx; the grid is the
+// number of pairs that can be resident at once (cudaOccupancyMaxActiveClusters,
+// queried once per device and instantiation), capped by the tile count.
+template <int BN, int STAGES, int ACC>
+int launch_tc2(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
+  using L = Mm2Layout<BN, STAGES, ACC>;
+  CUtensorMap ta, tb;
+  int s = ks::encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, uint64_t(a.k), uint64_t(a.m),
+                             uint64_t(a.k) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != KS_OK) return s;
+  s = ks::encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, uint64_t(a.n), uint64_t(a.k),
+                         uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != KS_OK) return s;
+  auto kern = matmul_tc2_kernel<BN, STAGES, ACC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t lc = {};
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = L::smem_request;
+  lc.stream = st;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  static std::atomic<int> max_pairs[64];  // per device; 0 = not queried yet
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return ks::map_cuda(e);
+  int pairs_max = dev < 64 ? max_pairs[dev].load(std::memory_order_relaxed) : 0;
+  if (pairs_max <= 0) {
+    lc.gridDim = dim3(2 * unsigned(ks::sm_count() / 2));
+    if ((e = cudaOccupancyMaxActiveClusters(&pairs_max, kern, &lc)) != cudaSuccess) return ks::map_cuda(e);
+    if (pairs_max <= 0) return KS_ERR_LAUNCH;
+    if (dev < 64) max_pairs[dev].store(pairs_max, std::memory_order_relaxed);
+  }
+  const int64_t tiles = ((a.m + 2 * kBM - 1) / (2 * kBM)) * ((a.n + BN - 1) / BN);
+  const int pairs = int(tiles < pairs_max ? tiles : pairs_max);
+  lc.gridDim = dim3(2 * unsigned(pairs));
+  e = cudaLaunchKernelEx(&lc, kern, ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n), int(a.k),
+                         cfg.group_m, ks::wait_ctx());
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  return ks::map_cuda(cudaGetLastError());
+}
+
+template <int BN, int ACC>
+int launch_tc2_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
+  switch (cfg.stages) {
+    case 2: return launch_tc2<BN, 2, ACC>(cfg, a, st);
+    case 3: return launch_tc2<BN, 3, ACC>(cfg, a, st);
+    case 4: return launch_tc2<BN, 4, ACC>(cfg, a, st);
+    case 5: return launch_tc2<BN, 5, ACC>(cfg, a, st);
+    case 6: return launch_tc2<BN, 6, ACC>(cfg, a, st);
+    default: return KS_ERR_INVALID_CONFIG;
+  }
+}
+
 // Stage counts instantiated per tile width (the ring must fit 227 KB).
 template <int BN>
 constexpr int max_stages() { return BN == 256 ? 4 : 6; }
@@ -322,8 +604,11 @@ int launch_tc_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaS
 
 constexpr uint32_t kSmemLimit = 227 * 1024;
 
-uint32_t smem_for(int bn, int stages) {
-  return uint32_t(stages) * (kABytes + uint32_t(kBK) * bn * 2) + (2 * stages + 5) * 8 + 16 + 1024;
+// Per-CTA bytes: A ring + B ring (half of tile_n per CTA for the pair
+// kernel) + barriers + alignment slack.
+uint32_t smem_for(int bm, int bn, int stages) {
+  const uint32_t b_cols = bm == 256 ? uint32_t(bn / 2) : uint32_t(bn);
+  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + (2 * stages + 5) * 8 + 16 + 1024;
 }
 
 }  // namespace
@@ -332,21 +617,26 @@ extern "C" {
 
 int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_t k, char *reason, size_t len) {
   if (!cfg) return KS_ERR_INVALID_ARGS;
-  if (cfg->tile_m != 128) {
-    ks::set_reason(reason, len, "matmul: tile_m must be 128 (one UMMA M=128 accumulator per CTA)");
+  if (cfg->tile_m != 128 && cfg->tile_m != 256) {
+    ks::set_reason(reason, len,
+                   "matmul: tile_m must be 128 (one CTA, UMMA M=128) or 256 (a CTA pair, cta_group::2 M=256)");
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256) {
     ks::set_reason(reason, len, "matmul: tile_n must be 64, 128 or 256 (sm_100a space)");
     return KS_ERR_INVALID_CONFIG;
   }
+  if (cfg->tile_m == 256 && cfg->tile_n == 64) {
+    ks::set_reason(reason, len, "matmul: tile_m 256 needs tile_n 128 or 256 (each CTA loads tile_n/2 >= 64 columns)");
+    return KS_ERR_INVALID_CONFIG;
+  }
   if (cfg->tile_k != 64) {
     ks::set_reason(reason, len, "matmul: tile_k must be 64 (one 128-byte swizzle row of bf16)");
     return KS_ERR_INVALID_CONFIG;
   }
-  if (cfg->stages < 2 || cfg->stages > (cfg->tile_n == 256 ? 4 : 6)) {
-    ks::set_reason(reason, len, "matmul: stages must be 2..%d for tile_n %d", cfg->tile_n == 256 ? 4 : 6,
-                   cfg->tile_n);
+  const int max_st = (cfg->tile_n == 256 && cfg->tile_m == 128) ? 4 : 6;
+  if (cfg->stages < 2 || cfg->stages > max_st) {
+    ks::set_reason(reason, len, "matmul: stages must be 2..%d for tile %dx%d", max_st, cfg->tile_m, cfg->tile_n);
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->acc_stages != 1 && cfg->acc_stages != 2) {
@@ -357,10 +647,10 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
     ks::set_reason(reason, len, "matmul: group_m must be 1..64");
     return KS_ERR_INVALID_CONFIG;
   }
-  const uint32_t smem = smem_for(cfg->tile_n, cfg->stages);
+  const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages);
   if (smem > kSmemLimit) {
-    ks::set_reason(reason, len, "matmul: %u bytes of shared memory for %d stages of 128x%dx64 > %u", smem,
-                   cfg->stages, cfg->tile_n, kSmemLimit);
+    ks::set_reason(reason, len, "matmul: %u bytes of shared memory for %d stages of %dx%dx64 > %u", smem,
+                   cfg->stages, cfg->tile_m, cfg->tile_n, kSmemLimit);
     return KS_ERR_INVALID_CONFIG;
   }
   if (m < 0 || n < 0 || k < 0) {
@@ -390,6 +680,10 @@ int ks_matmul_launch(const ks_matmul_config *cfg, const ks_matmul_args *a, void 
     return ks::map_cuda(cudaGetLastError());
   }
   const bool two = cfg->acc_stages == 2;
+  if (cfg->tile_m == 256) {
+    if (cfg->tile_n == 128) return two ? launch_tc2_stages<128, 2>(*cfg, *a, st) : launch_tc2_stages<128, 1>(*cfg, *a, st);
+    return two ? launch_tc2_stages<256, 2>(*cfg, *a, st) : launch_tc2_stages<256, 1>(*cfg, *a, st);
+  }
   switch (cfg->tile_n) {
     case 64: return two ? launch_tc_stages<64, 2>(*cfg, *a, st) : launch_tc_stages<64, 1>(*cfg, *a, st);
     case 128: return two ? launch_tc_stages<128, 2>(*cfg, *a, st) : launch_tc_stages<128, 1>(*cfg, *a, st);

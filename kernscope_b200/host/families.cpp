@@ -193,8 +193,8 @@ ks_matmul_config to_mm(const json &c) {
   return ks_matmul_config{iget(c, "tile_m", 128), iget(c, "tile_n", 256), iget(c, "tile_k", 64),
                           iget(c, "stages", 4),   iget(c, "acc_stages", 2), iget(c, "group_m", 8)};
 }
-json mm_json(int bn, int st, int acc, int g) {
-  return db::json::object({{"tile_m", json(128)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
+json mm_json(int bm, int bn, int st, int acc, int g) {
+  return db::json::object({{"tile_m", json(bm)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
                            {"stages", json(st)}, {"acc_stages", json(acc)}, {"group_m", json(g)}});
 }
 int pow2_cols(int c) {
@@ -252,16 +252,21 @@ class MatmulFamily : public Family {
   }
   std::vector<json> enumerate(bool full, const std::vector<std::int64_t> &) const override {
     std::vector<json> v;
+    // tile_m 128: one CTA per tile; tile_m 256: a CTA pair (cta_group::2)
     if (!full) {
       for (auto [bn, st] : {std::pair{256, 3}, {256, 4}, {128, 4}, {128, 6}})
         for (int acc : {1, 2})
-          for (int g : {8, 16}) v.push_back(mm_json(bn, st, acc, g));
+          for (int g : {8, 16}) v.push_back(mm_json(128, bn, st, acc, g));
+      for (int st : {4, 6})
+        for (int g : {8, 16}) v.push_back(mm_json(256, 256, st, 2, g));
       return v;
     }
-    for (int bn : {64, 128, 256})
-      for (int st = 2; st <= 6; ++st)
-        for (int acc : {1, 2})
-          for (int g : {1, 4, 8, 16, 32}) v.push_back(mm_json(bn, st, acc, g));
+    for (int bm : {128, 256})
+      for (int bn : {64, 128, 256})
+        for (int st = 2; st <= 6; ++st)
+          for (int acc : {1, 2})
+            for (int g : {1, 4, 8, 16, 32})
+              if (bm == 128 || bn != 64) v.push_back(mm_json(bm, bn, st, acc, g));
     return v;
   }
   ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
@@ -932,8 +937,10 @@ ConfigVerdict validate_config(const ReductionConfig &c, const ElemProblem &p) no
 }
 
 std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
-  // A ring (128 x 64 bf16) + B ring (64 x tile_n bf16) + barriers + 1 KB alignment slack
-  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * c.tile_n * 2) + (2 * c.stages + 2 * c.acc_stages + 1) * 8 +
+  // per CTA: A ring (128 x 64 bf16) + B ring (64 x tile_n bf16; half of tile_n
+  // for the CTA pair of tile_m 256) + barriers + 1 KB alignment slack
+  const std::int64_t b_cols = c.tile_m == 256 ? c.tile_n / 2 : c.tile_n;
+  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * b_cols * 2) + (2 * c.stages + 2 * c.acc_stages + 1) * 8 +
          16 + 1024;
 }
 
@@ -948,7 +955,8 @@ std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProbl
 LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) noexcept {
   LaunchGeometry g;
   const std::int64_t tiles = ((p.m + c.tile_m - 1) / c.tile_m) * ((p.n + c.tile_n - 1) / c.tile_n);
-  g.grid_x = int(std::min<std::int64_t>(tiles, 148));  // persistent: one CTA per SM
+  // persistent: one CTA per SM (tile_m 256: one CTA pair per two SMs)
+  g.grid_x = c.tile_m == 256 ? int(2 * std::min<std::int64_t>(tiles, 74)) : int(std::min<std::int64_t>(tiles, 148));
   g.block_x = 192;
   g.smem_bytes = int(smem_bytes(c));
   g.tmem_columns = pow2_cols(c.acc_stages * c.tile_n);

@@ -30,8 +30,9 @@ def ks(cuda_ok):
 
 
 def _configs(N):
-    for bn, st, acc in itertools.product((64, 128, 256), (2, 3, 4, 5, 6), (1, 2)):
-        cfg = N.MatmulConfig(128, bn, 64, st, acc, 8)
+    """Every tile/stage/accumulator config: one CTA (tile_m 128) and CTA pairs (tile_m 256)."""
+    for bm, bn, st, acc in itertools.product((128, 256), (64, 128, 256), (2, 3, 4, 5, 6), (1, 2)):
+        cfg = N.MatmulConfig(bm, bn, 64, st, acc, 8)
         if N.validate("matmul", cfg, 64, 64, 64)[0] == 0:
             yield cfg
 
@@ -83,7 +84,8 @@ def test_matmul_ragged(ks, shape):
     inp = oin.generate_inputs("matmul", shape, seed=3)
     exp = orf.matmul(inp["a"], inp["b"])
     a, b = to_torch(inp["a"]), to_torch(inp["b"])
-    for cfg in (N.MatmulConfig(128, 256, 64, 4, 2, 8), N.MatmulConfig(128, 64, 64, 3, 1, 1)):
+    for cfg in (N.MatmulConfig(128, 256, 64, 4, 2, 8), N.MatmulConfig(128, 64, 64, 3, 1, 1),
+                N.MatmulConfig(256, 256, 64, 5, 2, 16), N.MatmulConfig(256, 128, 64, 3, 1, 1)):
         assert_bf16_close(to_numpy(ops.matmul(a, b, cfg=cfg)), exp)
 
 
@@ -109,13 +111,15 @@ def test_matmul_empty(ks):
     assert float(out.abs().max()) == 0.0
 
 
-def test_matmul_8192_sampled(ks):
+@pytest.mark.parametrize("tile_m", [128, 256])
+def test_matmul_8192_sampled(ks, tile_m):
     """C4 8192^3 with N(0, 1/sqrt(K)) operands: a full 128-row panel and 4096
     random elements against an fp32 reference (rel-err <= 1e-2)."""
-    _, ops = ks
+    N, ops = ks
+    cfg = N.MatmulConfig(tile_m, 256, 64, 4 if tile_m == 128 else 5, 2, 16)
     m = n = k = 8192
     inp = oin.baseline_inputs("matmul", (m, n, k), seed=3)
-    y = ops.matmul(to_torch(inp["a"]), to_torch(inp["b"]))
+    y = ops.matmul(to_torch(inp["a"]), to_torch(inp["b"]), cfg=cfg)
     af, bf = inp["a"].astype(np.float32), inp["b"].astype(np.float32)
     r0 = 4096 + 64  # a panel that straddles two 128-row tiles
     panel = to_numpy(y[r0:r0 + 128])
@@ -132,3 +136,5 @@ def test_matmul_invalid_configs(ks):
     assert N.validate("matmul", N.MatmulConfig(64, 128, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 6, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(128, 96, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(256, 64, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 6, 2, 8), 64, 64, 64)[0] == 0

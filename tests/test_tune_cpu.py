@@ -31,9 +31,10 @@ def test_shape_hash_and_cache_key():
 
 def test_matmul_space():
     auto = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192])
-    assert len(auto) == 16 and all(v["valid"] for v in auto)
+    assert len(auto) == 20 and all(v["valid"] for v in auto)
+    assert sum(v["config"]["tile_m"] == 256 for v in auto) == 4
     full = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192], full=True)
-    assert len(full) == 150
+    assert len(full) == 250
     bad = [v for v in full if not v["valid"]]
     assert len(bad) == 20  # 5 and 6 stages of 128x256 tiles exceed 227 KB
     assert all("stages" in v["reason"] for v in bad)
