@@ -235,6 +235,26 @@ int ks_flash_attention_validate(const ks_flash_attention_config *cfg,
 int ks_flash_attention_launch(const ks_flash_attention_config *cfg,
                               const ks_flash_attention_args *args, void *stream);
 
+/* ---- roofline peak probes (libs/bench/kernels/peaks.hip, driven by
+ * tools/bench/main.cpp: kernscope-bench) ------------------------------------
+ * Each enqueues one kernel on `stream` and returns at once; time them with
+ * events.  `sink` is a device buffer of at least ks_peak_sink_words() 32-bit
+ * words (keeps the probes' results live).
+ *   ks_peak_copy:     dst <- src, `bytes` (multiple of 16, 16-byte aligned);
+ *                     HBM traffic = 2 * bytes.
+ *   ks_peak_read:     read-only sweep of `bytes`; traffic = bytes.
+ *   ks_peak_mma_bf16: one CTA per SM issuing `iters` x 4 tcgen05.mma
+ *                     (bf16 -> fp32, M=128, N=256, K=16) from shared memory;
+ *                     *flops = FLOPs of the launch.
+ *   ks_peak_ffma_f32: fp32 FMA chains; *flops = FLOPs of the launch.
+ *   ks_peak_smem:     16-byte shared-memory loads; *bytes = bytes read.     */
+int ks_peak_sink_words(size_t *words);
+int ks_peak_copy(void *dst, const void *src, size_t bytes, void *stream);
+int ks_peak_read(const void *src, size_t bytes, void *sink, void *stream);
+int ks_peak_mma_bf16(long long iters, void *sink, double *flops, void *stream);
+int ks_peak_ffma_f32(long long iters, void *sink, double *flops, void *stream);
+int ks_peak_smem(long long iters, void *sink, double *bytes, void *stream);
+
 /* ---- symbols --------------------------------------------------------------
  * Stable per-config kernel symbol (kernel_symbol(), e.g. matmul_gen.h:161),
  * written into buf.  family: "matmul", "flash_attention", "softmax",

@@ -145,6 +145,12 @@ PROTOTYPES = {
     "ks_flash_attention_validate": (C.c_int, [_P(FlashAttentionConfig), _P(FlashAttentionArgs), C.c_char_p,
                                               C.c_size_t]),
     "ks_flash_attention_launch": (C.c_int, [_P(FlashAttentionConfig), _P(FlashAttentionArgs), C.c_void_p]),
+    "ks_peak_sink_words": (C.c_int, [_P(C.c_size_t)]),
+    "ks_peak_copy": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ks_peak_read": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "ks_peak_mma_bf16": (C.c_int, [C.c_longlong, C.c_void_p, _P(C.c_double), C.c_void_p]),
+    "ks_peak_ffma_f32": (C.c_int, [C.c_longlong, C.c_void_p, _P(C.c_double), C.c_void_p]),
+    "ks_peak_smem": (C.c_int, [C.c_longlong, C.c_void_p, _P(C.c_double), C.c_void_p]),
     "ks_kernel_symbol": (C.c_int, [C.c_char_p, C.c_void_p, C.c_char_p, C.c_size_t]),
 }
 
