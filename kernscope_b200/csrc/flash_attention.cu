@@ -46,6 +46,15 @@ namespace {
 constexpr int kTile = 128;               // query rows per tile, K/V rows per tile
 constexpr int kD = 128;                  // head dim
 constexpr int kThreads = 320;            // 8 softmax warps + producer + MMA
+// The two-tile kernel runs three warpgroups: softmax (warps 0-3, 4-7) and a
+// third whose warps 8 and 9 are the producer and the MMA issuer.  Launched
+// at 168 registers per thread (65536 / 384, rounded to the allocation
+// granule), the third warpgroup gives registers back and the softmax
+// warpgroups take them: 128 x 56 + 256 x 216 = 62464 <= 384 x 168 = 64512,
+// so the increase never waits on registers the block does not hold.
+constexpr int kThreads2 = 384;
+constexpr int kRegsLow = 56, kRegsHigh = 216;
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads2 * 168, "register split exceeds the launch");
 constexpr uint32_t kBox = 128 * 64 * 2;  // [128 rows x 64 cols] bf16 box = 16 KB
 constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
 constexpr int kStages = 2;
@@ -137,7 +146,7 @@ KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool acc
                accumulate || kk > 0);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
                   float scale_log2, int causal, KsWait wait) {
@@ -203,91 +212,96 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ks_tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 8) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- producer
-      uint8_t *qs = smem + L::q_off;
-      ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
-      for (int g = 0; g < 2; ++g)
-        for (int h = 0; h < 2; ++h) ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64,
-                                                   q0 + g * kTile, bh);
-      uint32_t armed = 0, armed_par = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        if (!ks_mbar_wait(kv_empty + st, ph ^ 1u, abort, wait)) break;
-        uint8_t *ks = smem + L::k_off + st * kTileBytes;
-        uint8_t *vs = smem + L::v_off + st * kTileBytes;
-        ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
-        for (int h = 0; h < 2; ++h) ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, bh);
-        ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
-        for (int h = 0; h < 2; ++h) ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, bh);
-        armed |= 1u << st;
-        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+  // Registers move from the producer/MMA warpgroup to the softmax ones
+  // (warpgroup-uniform branches; the roles stay inside them).
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- producer
+        uint8_t *qs = smem + L::q_off;
+        ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+        for (int g = 0; g < 2; ++g)
+          for (int h = 0; h < 2; ++h) ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64,
+                                                     q0 + g * kTile, bh);
+        uint32_t armed = 0, armed_par = 0;
+        for (int j = 0; j < n_kv; ++j) {
+          const int st = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          if (!ks_mbar_wait(kv_empty + st, ph ^ 1u, abort, wait)) break;
+          uint8_t *ks = smem + L::k_off + st * kTileBytes;
+          uint8_t *vs = smem + L::v_off + st * kTileBytes;
+          ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
+          for (int h = 0; h < 2; ++h) ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, bh);
+          ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
+          for (int h = 0; h < 2; ++h) ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, bh);
+          armed |= 1u << st;
+          armed_par = (armed_par & ~(1u << st)) | (ph << st);
+        }
+        // teardown: the loads issued above have landed
+        ks_mbar_wait(q_full, 0, nullptr, wait);
+        for (int s = 0; s < kStages; ++s)
+          if (armed & (1u << s)) {
+            ks_mbar_wait(k_full + s, (armed_par >> s) & 1u, nullptr, wait);
+            ks_mbar_wait(v_full + s, (armed_par >> s) & 1u, nullptr, wait);
+          }
       }
-      // teardown: the loads issued above have landed
-      ks_mbar_wait(q_full, 0, nullptr, wait);
-      for (int s = 0; s < kStages; ++s)
-        if (armed & (1u << s)) {
-          ks_mbar_wait(k_full + s, (armed_par >> s) & 1u, nullptr, wait);
-          ks_mbar_wait(v_full + s, (armed_par >> s) & 1u, nullptr, wait);
-        }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
-      const uint32_t q_addr = ks_smem_u32(smem + L::q_off);
-      const uint32_t k_addr = ks_smem_u32(smem + L::k_off);
-      const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
-      const uint32_t t_s[2] = {tmem + 0, tmem + 128};
-      const uint32_t t_o[2] = {tmem + 256, tmem + 384};
-      bool ok = ks_mbar_wait(q_full, 0, abort, wait) && ks_mbar_wait(k_full, 0, abort, wait);
-      if (ok) {
-        ks_tc_fence_after();
-        issue_s(t_s[0], q_addr, k_addr);
-        ks_umma_commit(s_full + 0);
-        issue_s(t_s[1], q_addr + kTileBytes, k_addr);
-        ks_umma_commit(s_full + 1);
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int st1 = (j + 1) % kStages;
-        const uint32_t ph1 = ((j + 1) / kStages) & 1;
-        const bool more0 = j + 1 < n_t[0], more1 = j + 1 < n_kv;
-        if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
-        // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
-        if (j < n_t[0]) {
-          if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
+    } else if (warp == 9) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- MMA issuer
+        const uint32_t q_addr = ks_smem_u32(smem + L::q_off);
+        const uint32_t k_addr = ks_smem_u32(smem + L::k_off);
+        const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
+        const uint32_t t_s[2] = {tmem + 0, tmem + 128};
+        const uint32_t t_o[2] = {tmem + 256, tmem + 384};
+        bool ok = ks_mbar_wait(q_full, 0, abort, wait) && ks_mbar_wait(k_full, 0, abort, wait);
+        if (ok) {
           ks_tc_fence_after();
-          issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
-          if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
-        }
-        if (more1) {
-          if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
-          ks_tc_fence_after();
-        }
-        if (more0) {
-          issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
+          issue_s(t_s[0], q_addr, k_addr);
           ks_umma_commit(s_full + 0);
-        }
-        // tile 1
-        if (!ks_mbar_wait(p_full + 1, j & 1, abort, wait)) break;
-        ks_tc_fence_after();
-        issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0);
-        ks_umma_commit(kv_empty + st);
-        if (more1) {
-          issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
+          issue_s(t_s[1], q_addr + kTileBytes, k_addr);
           ks_umma_commit(s_full + 1);
-        } else {
-          ks_umma_commit(o_full + 1);
         }
+        for (int j = 0; j < n_kv && ok; ++j) {
+          const int st = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          const int st1 = (j + 1) % kStages;
+          const uint32_t ph1 = ((j + 1) / kStages) & 1;
+          const bool more0 = j + 1 < n_t[0], more1 = j + 1 < n_kv;
+          if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
+          // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
+          if (j < n_t[0]) {
+            if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
+            ks_tc_fence_after();
+            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
+            if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
+          }
+          if (more1) {
+            if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
+            ks_tc_fence_after();
+          }
+          if (more0) {
+            issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
+            ks_umma_commit(s_full + 0);
+          }
+          // tile 1
+          if (!ks_mbar_wait(p_full + 1, j & 1, abort, wait)) break;
+          ks_tc_fence_after();
+          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0);
+          ks_umma_commit(kv_empty + st);
+          if (more1) {
+            issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
+            ks_umma_commit(s_full + 1);
+          } else {
+            ks_umma_commit(o_full + 1);
+          }
+        }
+        ks_umma_commit(drain);
+        ks_mbar_wait(drain, 0, nullptr, wait);
       }
-      ks_umma_commit(drain);
-      ks_mbar_wait(drain, 0, nullptr, wait);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax
     const int g = warp >> 2;         // Q tile of this warpgroup
     const int qd = warp & 3;         // TMEM lane quadrant
@@ -862,7 +876,7 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
                                        int(FaLayout::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
   dim3 grid(unsigned((a->nq + 2 * kTile - 1) / (2 * kTile)), unsigned(bh));
-  fa_fwd_kernel<<<grid, kThreads, FaLayout::smem_request, st>>>(
+  fa_fwd_kernel<<<grid, kThreads2, FaLayout::smem_request, st>>>(
       tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), scale_log2, cfg->causal,
       ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());

@@ -473,7 +473,10 @@ class FlashFamily : public Family {
   Resources resources(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
     if (f.d != 128) return Resources{48, 4 * 256 * 4, 128, 0};
-    return Resources{168, int(smem_bytes(typed(cfg, causal), FlashAttentionProblem{})), 320, 512};
+    const FlashAttentionConfig c = typed(cfg, causal);
+    // tile_m 256: three warpgroups (the producer/MMA one hands registers to
+    // the two softmax ones); tile_m 128: ten warps
+    return Resources{168, int(smem_bytes(c, FlashAttentionProblem{})), c.tile_m == 256 ? 384 : 320, 512};
   }
   LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
@@ -967,7 +970,7 @@ LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttenti
   LaunchGeometry g;
   g.grid_x = int((p.nq + c.tile_m - 1) / c.tile_m);
   g.grid_y = int(p.batch_heads);
-  g.block_x = p.d == 128 ? 320 : 128;
+  g.block_x = p.d != 128 ? 128 : c.tile_m == 256 ? 384 : 320;
   if (p.d != 128) g.grid_x = int((p.nq + 3) / 4);
   g.smem_bytes = p.d == 128 ? int(smem_bytes(c, p)) : 4 * 256 * 4;
   g.tmem_columns = p.d == 128 ? 512 : 0;
