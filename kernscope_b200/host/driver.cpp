@@ -265,7 +265,8 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
   roofline::RooflinePosition pos;
   roofline::KernelFamily rk;
   roofline::family_from_name(fam_name, &rk);
-  roofline::roofline_position(rk, {}, bytes, std::max<std::int64_t>(flops, 1), opts.arch, &pos);
+  const bool roofline_ok = roofline::roofline_position(rk, {}, bytes, std::max<std::int64_t>(flops, 1), opts.arch,
+                                                       &pos) == roofline::ErrorCode::kNone;
   const bool tensor_bound = fam_name == "matmul" || fam_name == "flash_attention";
 
   // live device?
@@ -507,9 +508,13 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
     }
   std::vector<const Variant *> ord;
   for (const Variant &v : variants) ord.push_back(&v);
+  // report order (the reference's contract): measured variants by median,
+  // ties on p20 then p80, then the rest in enumeration order
   std::stable_sort(ord.begin(), ord.end(), [](const Variant *a, const Variant *b) {
     if (a->has_timings != b->has_timings) return a->has_timings;
     if (a->has_timings && a->median != b->median) return a->median < b->median;
+    if (a->has_timings && a->p20 != b->p20) return a->p20 < b->p20;
+    if (a->has_timings && a->p80 != b->p80) return a->p80 < b->p80;
     return a->index < b->index;
   });
   std::vector<Value> vars;
@@ -533,8 +538,7 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
                                      {"norm_rel_err", Value(v.gate.norm_rel_err)},
                                      {"criterion", Value(v.gate.criterion)}}));
     if (v.has_timings) {
-      m.emplace_back("timings", object({{"median_ms", Value(v.median)}, {"p20_ms", Value(v.p20)},
-                                        {"p80_ms", Value(v.p80)}}));
+      m.emplace_back("timings", object({{"median", Value(v.median)}, {"p20", Value(v.p20)}, {"p80", Value(v.p80)}}));
       const double a = achieved(v.median);
       m.emplace_back(tensor_bound ? "achieved_tflops" : "achieved_gbps", Value(a));
       m.emplace_back("roofline_achieved", Value(peak_unit > 0 ? a / peak_unit : 0.0));
@@ -542,28 +546,41 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
     vars.push_back(Value(std::move(m)));
   }
   Value best_v;
+  double best_occ = 0.0;
+  std::string best_limiter;
   if (out.has_best) {
     const double a = achieved(out.best_median_ms);
-    best_v = object({{"config", out.best_config}, {"symbol", Value(out.best_symbol)},
-                     {"median_ms", Value(out.best_median_ms)}, {"p20_ms", Value(out.best_p20_ms)},
-                     {"p80_ms", Value(out.best_p80_ms)},
-                     {tensor_bound ? "achieved_tflops" : "achieved_gbps", Value(a)},
-                     {"roofline_achieved", Value(peak_unit > 0 ? a / peak_unit : 0.0)},
-                     {"speedup_vs_baseline", Value(baseline_median > 0 ? baseline_median / out.best_median_ms : 1.0)}});
+    std::vector<Value::Member> bm{{"config", out.best_config}, {"symbol", Value(out.best_symbol)},
+                                  {"timings", object({{"median", Value(out.best_median_ms)},
+                                                      {"p20", Value(out.best_p20_ms)},
+                                                      {"p80", Value(out.best_p80_ms)}})},
+                                  {tensor_bound ? "achieved_tflops" : "achieved_gbps", Value(a)},
+                                  {"roofline_achieved", Value(peak_unit > 0 ? a / peak_unit : 0.0)}};
+    for (const Variant &v : variants)
+      if (v.best) {
+        best_occ = v.occupancy;
+        best_limiter = v.limiter;
+        if (v.gated)
+          bm.emplace_back("gate", object({{"shape", Value(v.gate_shape)}, {"grid", Value(v.gate_grid)},
+                                          {"block", Value(v.gate_block)}, {"symbol", Value(v.symbol)}}));
+      }
+    best_v = Value(std::move(bm));
   }
   std::vector<Value> sh;
   for (auto d : opts.shape) sh.emplace_back(double(d));
   std::vector<Value> gsh;
   for (auto d : gate_shape) gsh.emplace_back(double(d));
   const Value ev = object({
-      {"tool", Value(kToolVersion)},
+      {"schema_version", Value(1)},
+      {"tool_version", Value(kToolVersion)},
       {"kernel_family", Value(fam_name)},
-      {"arch", Value(opts.arch)},
+      {"gpu_arch", Value(opts.arch)},
       {"shape", Value(sh)},
       {"gate_shape", Value(gsh)},
       {"shape_hash", Value(out.shape_hash)},
       {"cache_key", Value(out.cache_key)},
-      {"grid", Value(opts.grid_preset)},
+      {"grid_preset", Value(opts.grid_preset)},
+      {"grid_size", Value(out.variants_total)},
       {"min_occupancy", Value(opts.min_occupancy)},
       {"n_gpus", Value(1)},
       {"live", Value(want_live)},
@@ -572,22 +589,35 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
       {"summary", object({{"variants_total", Value(out.variants_total)},
                           {"prescreen_rejected", Value(out.prescreen_rejected)},
                           {"compile_failed", Value(out.compile_failed)},
-                          {"golden_failed", Value(out.golden_failed)},
+                          {"golden_gate_failed", Value(out.golden_failed)},
                           {"bench_failed", Value(out.bench_failed)},
                           {"benchmarked", Value(out.benchmarked)},
                           {"cached", Value(out.cached)},
-                          {"compiled", Value(out.compiled)}})},
-      {"roofline", object({{"flops", Value(double(flops))},
+                          {"compiled", Value(out.compiled)},
+                          {"verifier_gated", Value(0)}})},
+      {"roofline", object({{"ok", Value(roofline_ok)},
+                           {"family", Value(fam_name)},
+                           {"flops", Value(double(flops))},
                            {"bytes_moved", Value(double(bytes))},
                            {"arithmetic_intensity", Value(pos.arithmetic_intensity)},
                            {"ridge_point", Value(pos.ridge_point)},
+                           {"bound_class", Value(roofline::bound_class_name(pos.bound_class))},
                            {"bound", Value(roofline::bound_class_name(pos.bound_class))},
+                           {"position", Value(pos.compute_bound_ceiling > 0
+                                                  ? pos.attained_flops / pos.compute_bound_ceiling
+                                                  : 0.0)},
+                           {"compute_bound_ceiling", Value(pos.compute_bound_ceiling)},
+                           {"memory_bound_ceiling", Value(pos.memory_bound_ceiling)},
+                           {"attained_flops", Value(pos.attained_flops)},
                            {"peak", Value(peak_unit)},
                            {"peak_unit", Value(tensor_bound ? "TFLOP/s" : "GB/s")},
                            {"peak_provenance", Value(peak.provenance)},
                            {"projected", Value(peak.projected)}})},
       {"best", best_v},
-      {"baseline", object({{"config", baseline_cfg}, {"median_ms", Value(baseline_median)}})},
+      {"occupancy", Value(best_occ)},
+      {"occupancy.limiter", Value(best_limiter)},
+      {"speedup", Value(baseline_median > 0 && out.best_median_ms > 0 ? baseline_median / out.best_median_ms : 0.0)},
+      {"baseline", object({{"config", baseline_cfg}, {"timings", object({{"median", Value(baseline_median)}})}})},
       {"variants", Value(std::move(vars))},
       {"db", object({{"path", Value(opts.db_path)}, {"records", Value(db_records)}, {"ok", Value(db_ok)}})},
       {"cache", object({{"path", Value(opts.cache_path)}, {"warning", Value(cache_warning)},

@@ -49,19 +49,19 @@ bool parse_shape(const std::string &s, std::vector<std::int64_t> *out) {
 void print_text(const kernscope::db::json::Value &ev) {
   using kernscope::db::json::Value;
   std::printf("kernscope-tune  family=%s  arch=%s  status=%s\n", ev.string_or("kernel_family", "").c_str(),
-              ev.string_or("arch", "").c_str(), ev.string_or("status", "").c_str());
+              ev.string_or("gpu_arch", "").c_str(), ev.string_or("status", "").c_str());
   std::printf("%s\n", ev.string_or("message", "").c_str());
   if (const Value *s = ev.find("summary"))
     std::printf("variants %d  prescreen-rejected %d  golden-failed %d  benchmarked %d  cached %d\n",
                 int(s->number_or("variants_total", 0)), int(s->number_or("prescreen_rejected", 0)),
-                int(s->number_or("golden_failed", 0)), int(s->number_or("benchmarked", 0)),
+                int(s->number_or("golden_gate_failed", 0)), int(s->number_or("benchmarked", 0)),
                 int(s->number_or("cached", 0)));
   if (const Value *vs = ev.find("variants"))
     for (const Value &v : vs->as_array()) {
       const Value *t = v.find("timings");
       std::printf("  %c %-52s %-20s %10s\n", v.find("best") && v.find("best")->as_bool() ? '*' : ' ',
                   v.string_or("symbol", "").c_str(), v.string_or("status", "").c_str(),
-                  t ? (std::to_string(t->number_or("median_ms", 0) * 1000.0).substr(0, 9) + "us").c_str() : "");
+                  t ? (std::to_string(t->number_or("median", 0) * 1000.0).substr(0, 9) + "us").c_str() : "");
     }
 }
 
@@ -71,14 +71,14 @@ void print_html(const kernscope::db::json::Value &ev) {
               ev.string_or("kernel_family", "").c_str());
   std::printf("<h1>kernscope-tune: %s on %s</h1><p>%s</p>\n<table border=\"1\"><tr><th>best</th><th>symbol</th>"
               "<th>status</th><th>median ms</th><th>reason</th></tr>\n",
-              ev.string_or("kernel_family", "").c_str(), ev.string_or("arch", "").c_str(),
+              ev.string_or("kernel_family", "").c_str(), ev.string_or("gpu_arch", "").c_str(),
               ev.string_or("message", "").c_str());
   if (const Value *vs = ev.find("variants"))
     for (const Value &v : vs->as_array()) {
       const Value *t = v.find("timings");
       std::printf("<tr><td>%s</td><td>%s</td><td>%s</td><td>%s</td><td>%s</td></tr>\n",
                   v.find("best") && v.find("best")->as_bool() ? "*" : "", v.string_or("symbol", "").c_str(),
-                  v.string_or("status", "").c_str(), t ? std::to_string(t->number_or("median_ms", 0)).c_str() : "",
+                  v.string_or("status", "").c_str(), t ? std::to_string(t->number_or("median", 0)).c_str() : "",
                   v.string_or("reason", "").c_str());
     }
   std::printf("</table><pre>%s</pre></body></html>\n", ev.dump().c_str());
