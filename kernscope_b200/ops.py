@@ -183,3 +183,63 @@ def device_error_take() -> int:
     w = C.c_int(0)
     N.check("ks_device_error_take", N.lib.ks_device_error_take(C.byref(w)))
     return w.value
+
+
+def _copy(dst: torch.Tensor, src: torch.Tensor, stream) -> None:
+    """One async copy through the C ABI (pinned host <-> device, either way)."""
+    n = src.numel() * src.element_size()
+    sp = _stream_ptr(stream)
+    if dst.is_cuda:
+        N.check("ks_gpu_memcpy_htod", N.lib.ks_gpu_memcpy_htod(C.c_void_p(dst.data_ptr()),
+                                                               C.c_void_p(src.data_ptr()), n, sp))
+    else:
+        N.check("ks_gpu_memcpy_dtoh", N.lib.ks_gpu_memcpy_dtoh(C.c_void_p(dst.data_ptr()),
+                                                               C.c_void_p(src.data_ptr()), n, sp))
+
+
+class HostRowPipeline:
+    """Row-wise families on host-resident data: rows move in chunks through
+    three streams -- host-to-device copy, kernel, device-to-host copy -- so the
+    copy of one chunk's input, the kernel on the previous chunk and the copy
+    of an earlier chunk's output overlap (PCIe moves both directions at once).
+
+    ``step(host_in, dev_in, host_out, dev_out, launch)`` runs one pass over all
+    rows: ``host_in`` / ``dev_in`` are matching [rows, ...] tensors (pinned
+    host, device), ``launch(r0, r1, stream)`` enqueues the family on rows
+    [r0, r1) of the device tensors, and the result lands in ``host_out``.
+    Consecutive steps pipeline as well; a chunk's device buffers are reused
+    only after the previous step's kernel and output copy are done with them.
+    Returns an event that completes when this step's output is on the host.
+    """
+
+    def __init__(self, rows: int, chunk_rows: int = 512):
+        self.chunks = [(r, min(rows, r + chunk_rows)) for r in range(0, rows, max(1, chunk_rows))]
+        self.s_in, self.s_k, self.s_out = (torch.cuda.Stream() for _ in range(3))
+        self.ev_k = [None] * len(self.chunks)
+        self.ev_out = [None] * len(self.chunks)
+
+    def step(self, host_in, dev_in, host_out, dev_out, launch):
+        for i, (r0, r1) in enumerate(self.chunks):
+            if self.ev_k[i] is not None:
+                self.s_in.wait_event(self.ev_k[i])  # the last step's kernel has read this chunk
+            for h, d in zip(host_in, dev_in):
+                _copy(d[r0:r1], h[r0:r1], self.s_in)
+            e_in = torch.cuda.Event()
+            e_in.record(self.s_in)
+            self.s_k.wait_event(e_in)
+            if self.ev_out[i] is not None:
+                self.s_k.wait_event(self.ev_out[i])  # the last step's output copy has read this chunk
+            launch(r0, r1, self.s_k)
+            self.ev_k[i] = torch.cuda.Event()
+            self.ev_k[i].record(self.s_k)
+            self.s_out.wait_event(self.ev_k[i])
+            _copy(host_out[r0:r1], dev_out[r0:r1], self.s_out)
+            self.ev_out[i] = torch.cuda.Event()
+            self.ev_out[i].record(self.s_out)
+        return self.ev_out[-1]
+
+    def join(self, stream=None) -> None:
+        """Make `stream` (default: current) wait for everything enqueued."""
+        s = stream if stream is not None else torch.cuda.current_stream()
+        for st in (self.s_in, self.s_k, self.s_out):
+            s.wait_stream(st)

@@ -167,3 +167,27 @@ def test_bias_gelu_ragged_total(ks):
         idx = np.arange(total)
         exp = orf.gelu_erf(orf.to_bf16(xflat.astype(np.float32) + inp["bias"][idx % cols].astype(np.float32)))
         assert_bf16_close(to_numpy(out), exp)
+
+
+@pytest.mark.parametrize("rows,chunk", [(4096, 512), (1000, 333), (7, 64)])
+def test_host_row_pipeline_matches_device(ks, rows, chunk):
+    """Row chunks through the three-stream host pipeline give the same bytes
+    as one device launch, over two pipelined steps with new host data."""
+    import torch
+
+    _, ops = ks
+    cols = 4096
+    pipe = ops.HostRowPipeline(rows, chunk_rows=chunk)
+    x_dev = torch.empty((rows, cols), dtype=torch.bfloat16, device="cuda")
+    y_dev = torch.empty_like(x_dev)
+    outs = []
+    hosts = [(torch.randn(rows, cols) * (s + 1)).bfloat16().pin_memory() for s in range(2)]
+    host_out = [torch.empty((rows, cols), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for s in range(2):
+        pipe.step([hosts[s]], [x_dev], host_out[s], y_dev,
+                  lambda r0, r1, st: ops.softmax(x_dev[r0:r1], out=y_dev[r0:r1], stream=st))
+    pipe.join()
+    torch.cuda.synchronize()
+    for s in range(2):
+        ref = ops.softmax(hosts[s].cuda()).cpu()
+        assert torch.equal(host_out[s], ref)
