@@ -12,7 +12,9 @@
   pre-screen, arch/occupancy/roofline models, bench, db + tunecache, driver,
   CLI), linked against the kernel library;
 * ``kernscope_b200/lib/kernscope-bench`` -- the roofline peak measurement
-  CLI (HBM, bf16 tensor, fp32, shared memory).
+  CLI (HBM, bf16 tensor, fp32, shared memory);
+* ``kernscope_b200/lib/ks-template-runner`` -- runs one kernel on raw host
+  buffers (the gate runner of the reference's template flow).
 
 Objects are rebuilt only when a source or header is newer than the object.
 """
@@ -40,6 +42,7 @@ KERNEL_LIB = os.path.join(LIBDIR, "libkernscope_b200.so")
 TUNE_LIB = os.path.join(LIBDIR, "libkernscope_tune.so")
 TUNE_CLI = os.path.join(LIBDIR, "kernscope-tune")
 BENCH_CLI = os.path.join(LIBDIR, "kernscope-bench")
+RUNNER_CLI = os.path.join(LIBDIR, "ks-template-runner")
 
 
 def _newer(target: str, deps) -> bool:
@@ -87,10 +90,11 @@ def build_tuner(force: bool) -> None:
     if not srcs:
         return
     hdrs = sorted(glob.glob(os.path.join(HOST, "*.h"))) + [os.path.join(INCLUDE, "kernscope_b200.h")]
-    clis = ("tune_cli.cpp", "bench_cli.cpp")
+    clis = ("tune_cli.cpp", "bench_cli.cpp", "runner_cli.cpp")
     lib_srcs = [s for s in srcs if not s.endswith(clis)]
     cli_src = [s for s in srcs if s.endswith("tune_cli.cpp")]
     bench_src = [s for s in srcs if s.endswith("bench_cli.cpp")]
+    runner_src = [s for s in srcs if s.endswith("runner_cli.cpp")]
     # The system g++ (nvcc's host compiler): both libraries must share one
     # dynamic libstdc++ (a toolchain that links libstdc++ statically would put
     # a second copy in the process next to the one the kernel library uses).
@@ -100,7 +104,7 @@ def build_tuner(force: bool) -> None:
     if force or _newer(TUNE_LIB, lib_srcs + hdrs + [KERNEL_LIB]):
         _run([cxx, *common, "-shared", *lib_srcs, "-o", TUNE_LIB, "-L", LIBDIR, "-lkernscope_b200",
               rpath, "-ldl", "-lpthread"])
-    for src, out in ((cli_src, TUNE_CLI), (bench_src, BENCH_CLI)):
+    for src, out in ((cli_src, TUNE_CLI), (bench_src, BENCH_CLI), (runner_src, RUNNER_CLI)):
         if src and (force or _newer(out, src + hdrs + [TUNE_LIB])):
             _run([cxx, *common, *src, "-o", out, "-L", LIBDIR, "-lkernscope_tune", "-lkernscope_b200",
                   rpath, "-ldl", "-lpthread"])
