@@ -65,8 +65,8 @@ struct FaLayout {
   static constexpr uint32_t k_off = q_off + 2 * kTileBytes;      // K[stages]
   static constexpr uint32_t v_off = k_off + kStages * kTileBytes;  // V[stages]
   static constexpr uint32_t bar_off = v_off + kStages * kTileBytes;
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain
-  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain, p_half[2]
+  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1 + 2;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t smem_request = bytes + 1024;
@@ -138,10 +138,11 @@ KS_DEV void issue_s(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
 // P comes from TMEM (8 columns = 16 bf16 per step); V is MN-major: two
 // 64-column boxes 16 KB apart (LBO), 8 key-rows 1024 bytes apart (SBO),
 // 16 key-rows = 2048 bytes per step.
-KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate, int kk0 = 0,
+                     int kk1 = kTile / 16) {
   constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, true);
 #pragma unroll
-  for (int kk = 0; kk < kTile / 16; ++kk)
+  for (int kk = kk0; kk < kk1; ++kk)
     ks_umma_ts(o_tmem, p_tmem + kk * 8, ks_umma_desc_sw128(v_addr + kk * 2048, kBox, 1024), idesc,
                accumulate || kk > 0);
 }
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t *p_full = s_full + 2;
   uint64_t *o_full = p_full + 2;
   uint64_t *drain = o_full + 2;
+  uint64_t *p_half = drain + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
 
@@ -194,6 +196,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     for (int g = 0; g < 2; ++g) {
       ks_mbar_init(s_full + g, 1);
       ks_mbar_init(p_full + g, 4);
+      ks_mbar_init(p_half + g, 4);
     }
     ks_mbar_init(o_full + 0, 1);
     ks_mbar_init(o_full + 1, 1);
@@ -271,9 +274,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
           // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
           if (j < n_t[0]) {
+            // the first half of P (keys 0-63) is read while the softmax stores the second
+            if (!ks_mbar_wait(p_half + 0, j & 1, abort, wait)) break;
+            ks_tc_fence_after();
+            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0, 0, 4);
             if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
             ks_tc_fence_after();
-            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0);
+            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, true, 4, 8);
             if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
           }
           if (more1) {
@@ -285,9 +292,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
             ks_umma_commit(s_full + 0);
           }
           // tile 1
+          if (!ks_mbar_wait(p_half + 1, j & 1, abort, wait)) break;
+          ks_tc_fence_after();
+          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0, 0, 4);
           if (!ks_mbar_wait(p_full + 1, j & 1, abort, wait)) break;
           ks_tc_fence_after();
-          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0);
+          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, true, 4, 8);
           ks_umma_commit(kv_empty + st);
           if (more1) {
             issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
@@ -371,11 +381,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
       F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
       const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
-      // P in two halves of 64 keys (32 packed columns each), stored as soon as
-      // computed: the S columns they overwrite are already in registers
+      // P in two halves of 64 keys (32 packed columns each), stored over S
+      // columns already in registers.  The first half is announced (p_half)
+      // once the second is computed, so the tensor core starts O += P V on
+      // keys 0-63 while the second half is stored.
+      uint32_t p[2][32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t p[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int e0 = 64 * half + 2 * c;
@@ -383,13 +395,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
           const F2 x = fma2(F2{__uint_as_float(r[e0]), __uint_as_float(r[e0 + 1])}, sc2, nm2);
           const F2 e{ex2(x.x), ex2(x.y)};
           rsum[c & 3] = add2(rsum[c & 3], e);
-          p[c] = ks_pack_bf16x2(e.x, e.y);
+          p[half][c] = ks_pack_bf16x2(e.x, e.y);
         }
-        if (half == 0)
-          ks_tmem_st32_at<0>(lane_addr + s_col + 0, p);
-        else
-          ks_tmem_st32_at<0>(lane_addr + s_col + 32, p);
+        if (half == 0) ks_tmem_st32_at<0>(lane_addr + s_col + 0, p[0]);
       }
+      ks_tmem_wait_st();
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(p_half + g);
+      ks_tmem_st32_at<0>(lane_addr + s_col + 32, p[1]);
       const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
       const float rs = rs2.x + rs2.y;
       l += rs;
