@@ -32,8 +32,10 @@
 //     exp2(s - m) stay <= 256, exact in fp32/bf16 range); the final O / l is
 //     rounded to bf16 once and stored;
 //   * causal: tile 0 stops one K/V tile before tile 1 (its last tile is fully
-//     masked) and its epilogue starts while tile 1's last MMAs run; heavy
-//     (late) query blocks launch first for load balance.
+//     masked) and its epilogue starts while tile 1's last MMAs run;
+//   * persistent: one CTA per SM walks (query block, head) work items, the
+//     heaviest query blocks of a head first; the next item's Q load and
+//     first QK^T MMAs overlap the current item's epilogue.
 //
 // All waits are bounded (KsWait); teardown waits for outstanding TMA loads
 // and MMAs before TMEM is freed.
@@ -50,10 +52,11 @@ constexpr int kThreads = 320;            // 8 softmax warps + producer + MMA
 // third whose warps 8 and 9 are the producer and the MMA issuer.  Launched
 // at 168 registers per thread (65536 / 384, rounded to the allocation
 // granule), the third warpgroup gives registers back and the softmax
-// warpgroups take them: 128 x 56 + 256 x 216 = 62464 <= 384 x 168 = 64512,
-// so the increase never waits on registers the block does not hold.
+// warpgroups take them: 128 x 88 + 256 x 208 = 64512 <= 384 x 168 = 64512,
+// so the increase never waits on registers the block does not hold (88 keeps
+// the persistent producer/MMA state, 208 the softmax row, free of spills).
 constexpr int kThreads2 = 384;
-constexpr int kRegsLow = 56, kRegsHigh = 216;
+constexpr int kRegsLow = 88, kRegsHigh = 208;
 static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads2 * 168, "register split exceeds the launch");
 constexpr uint32_t kBox = 128 * 64 * 2;  // [128 rows x 64 cols] bf16 box = 16 KB
 constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
@@ -65,8 +68,9 @@ struct FaLayout {
   static constexpr uint32_t k_off = q_off + 2 * kTileBytes;      // K[stages]
   static constexpr uint32_t v_off = k_off + kStages * kTileBytes;  // V[stages]
   static constexpr uint32_t bar_off = v_off + kStages * kTileBytes;
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain, p_half[2]
-  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1 + 2;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain, p_half[2],
+  // o_empty[2], q_empty
+  static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1 + 2 + 2 + 1;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t smem_request = bytes + 1024;
@@ -174,10 +178,44 @@ KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool acc
                accumulate || kk > 0);
 }
 
+// Work item k of CTA c (persistent grid of G CTAs): items are (256-query
+// block, batch*head) pairs ordered heaviest causal block first; round r hands
+// CTA c item r*G + c on even rounds and r*G + (G-1-c) on odd ones, which
+// evens out the per-CTA load of the decreasing causal item sizes.
+struct FaItem {
+  int q0, bh, n_kv, n_t0;
+};
+KS_DEV bool fa_item(int r, int c, int G, int num_items, int num_qb, int n_bh, int nq, int nk, int causal,
+                    FaItem &it) {
+  const int w = r * G + ((r & 1) ? G - 1 - c : c);
+  if (w >= num_items) return false;
+  // consecutive items share a head (its K/V stays in L2 while the CTAs
+  // running them stream it), heaviest query block of the head first
+  const int qb = num_qb - 1 - w % num_qb;
+  it.bh = w / num_qb;
+  it.q0 = qb * 2 * kTile;
+  int n_kv = (nk + kTile - 1) / kTile;
+  // tile g needs K/V tiles [0, n_t[g]); n_kv = n_t[1] >= n_t[0].  Under the
+  // causal mask tile 0 stops one K/V tile earlier (its last one is masked).
+  int n_t0 = n_kv;
+  if (causal) {
+    n_t0 = min(n_kv, (it.q0 + kTile - 1) / kTile + 1);
+    const int q_last = min(it.q0 + 2 * kTile, nq) - 1;
+    n_kv = min(n_kv, q_last / kTile + 1);
+    n_t0 = min(n_t0, n_kv);
+  }
+  it.n_kv = n_kv;
+  it.n_t0 = n_t0;
+  return true;
+}
+
+// Persistent: one CTA per SM walks its work items; the next item's Q load
+// and first QK^T MMAs run while the softmax warpgroups finish the current
+// item's epilogue.  Phases of the per-step barriers continue across items.
 __global__ void __launch_bounds__(kThreads2, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
-                  float scale_log2, int causal, KsWait wait) {
+                  int n_bh, float scale_log2, int causal, KsWait wait) {
   using L = FaLayout;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
@@ -192,29 +230,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t *o_full = p_full + 2;
   uint64_t *drain = o_full + 2;
   uint64_t *p_half = drain + 1;
+  uint64_t *o_empty = p_half + 2;
+  uint64_t *q_empty = o_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_qb = (nq + 2 * kTile - 1) / (2 * kTile);
-  const int qb = num_qb - 1 - int(blockIdx.x);  // heaviest causal blocks first
-  const int bh = blockIdx.y;
-  const int q0 = qb * 2 * kTile;
-  // number of K/V tiles this block needs
-  int n_kv = (nk + kTile - 1) / kTile;
-  // tile g needs K/V tiles [0, n_t[g]); n_kv = n_t[1] >= n_t[0].  Under the
-  // causal mask tile 0 stops one K/V tile earlier (its last one is masked).
-  int n_t[2] = {n_kv, n_kv};
-  if (causal) {
-    n_t[0] = min(n_kv, (q0 + kTile - 1) / kTile + 1);
-    const int q_last = min(q0 + 2 * kTile, nq) - 1;
-    n_kv = min(n_kv, q_last / kTile + 1);
-    n_t[1] = n_kv;
-    n_t[0] = min(n_t[0], n_kv);
-  }
+  const int num_items = num_qb * n_bh;
+  const int cta = int(blockIdx.x), G = int(gridDim.x);
 
   if (threadIdx.x == 0) {
     ks_mbar_init(q_full, 1);
+    ks_mbar_init(q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       ks_mbar_init(k_full + s, 1);
       ks_mbar_init(v_full + s, 1);
@@ -224,9 +252,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       ks_mbar_init(s_full + g, 1);
       ks_mbar_init(p_full + g, 4);
       ks_mbar_init(p_half + g, 4);
+      ks_mbar_init(o_full + g, 1);
+      ks_mbar_init(o_empty + g, 4);
     }
-    ks_mbar_init(o_full + 0, 1);
-    ks_mbar_init(o_full + 1, 1);
     ks_mbar_init(drain, 1);
     *abort = 0;
     ks_fence_mbar_init();
@@ -250,26 +278,41 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (lane == 0) {
         // ---------------------------------------------------------- producer
         uint8_t *qs = smem + L::q_off;
-        ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
-        for (int g = 0; g < 2; ++g)
-          for (int h = 0; h < 2; ++h) ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64,
-                                                     q0 + g * kTile, bh);
         uint32_t armed = 0, armed_par = 0;
-        for (int j = 0; j < n_kv; ++j) {
-          const int st = j % kStages;
-          const uint32_t ph = (j / kStages) & 1;
-          if (!ks_mbar_wait(kv_empty + st, ph ^ 1u, abort, wait)) break;
-          uint8_t *ks = smem + L::k_off + st * kTileBytes;
-          uint8_t *vs = smem + L::v_off + st * kTileBytes;
-          ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
-          for (int h = 0; h < 2; ++h) ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, bh);
-          ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
-          for (int h = 0; h < 2; ++h) ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, bh);
-          armed |= 1u << st;
-          armed_par = (armed_par & ~(1u << st)) | (ph << st);
+        int gj = 0;       // K/V tiles loaded so far (ring position)
+        int q_loads = 0;  // Q tile pairs loaded so far
+        bool ok = true;
+        FaItem it;
+        for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+          // the previous item's last QK^T MMA has read Q
+          if (r > 0 && !ks_mbar_wait(q_empty, (r - 1) & 1, abort, wait)) break;
+          ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+          for (int g = 0; g < 2; ++g)
+            for (int h = 0; h < 2; ++h)
+              ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64, it.q0 + g * kTile, it.bh);
+          ++q_loads;
+          for (int j = 0; j < it.n_kv; ++j, ++gj) {
+            const int st = gj % kStages;
+            const uint32_t ph = (gj / kStages) & 1;
+            if (!ks_mbar_wait(kv_empty + st, ph ^ 1u, abort, wait)) {
+              ok = false;
+              break;
+            }
+            uint8_t *ks = smem + L::k_off + st * kTileBytes;
+            uint8_t *vs = smem + L::v_off + st * kTileBytes;
+            ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
+            for (int h = 0; h < 2; ++h)
+              ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, it.bh);
+            ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
+            for (int h = 0; h < 2; ++h)
+              ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, it.bh);
+            armed |= 1u << st;
+            armed_par = (armed_par & ~(1u << st)) | (ph << st);
+          }
         }
-        // teardown: the loads issued above have landed
-        ks_mbar_wait(q_full, 0, nullptr, wait);
+        // teardown: the loads issued above have landed (the last Q and the
+        // last K/V of each ring stage)
+        if (q_loads > 0) ks_mbar_wait(q_full, (q_loads - 1) & 1, nullptr, wait);
         for (int s = 0; s < kStages; ++s)
           if (armed & (1u << s)) {
             ks_mbar_wait(k_full + s, (armed_par >> s) & 1u, nullptr, wait);
@@ -284,53 +327,72 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
         const uint32_t t_s[2] = {tmem + 0, tmem + 128};
         const uint32_t t_o[2] = {tmem + 256, tmem + 384};
-        bool ok = ks_mbar_wait(q_full, 0, abort, wait) && ks_mbar_wait(k_full, 0, abort, wait);
-        if (ok) {
+        int gj = 0;           // K/V tiles consumed so far (ring position)
+        int sg[2] = {0, 0};   // steps of each tile so far (s_full / p_half / p_full phases)
+        bool ok = true;
+        FaItem it;
+        for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+          const int n_t[2] = {it.n_t0, it.n_kv};
+          if (!ks_mbar_wait(q_full, r & 1, abort, wait) ||
+              !ks_mbar_wait(k_full + gj % kStages, (gj / kStages) & 1, abort, wait))
+            break;
           ks_tc_fence_after();
-          issue_s(t_s[0], q_addr, k_addr);
+          issue_s(t_s[0], q_addr, k_addr + (gj % kStages) * kTileBytes);
           ks_umma_commit(s_full + 0);
-          issue_s(t_s[1], q_addr + kTileBytes, k_addr);
+          issue_s(t_s[1], q_addr + kTileBytes, k_addr + (gj % kStages) * kTileBytes);
           ks_umma_commit(s_full + 1);
-        }
-        for (int j = 0; j < n_kv && ok; ++j) {
-          const int st = j % kStages;
-          const uint32_t ph = (j / kStages) & 1;
-          const int st1 = (j + 1) % kStages;
-          const uint32_t ph1 = ((j + 1) / kStages) & 1;
-          const bool more0 = j + 1 < n_t[0], more1 = j + 1 < n_kv;
-          if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
-          // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
-          if (j < n_t[0]) {
-            // the first half of P (keys 0-63) is read while the softmax stores the second
-            if (!ks_mbar_wait(p_half + 0, j & 1, abort, wait)) break;
+          if (it.n_kv == 1) ks_umma_commit(q_empty);  // that was the item's last read of Q
+          for (int j = 0; j < it.n_kv && ok; ++j, ++gj) {
+            const int st = gj % kStages;
+            const uint32_t ph = (gj / kStages) & 1;
+            const int st1 = (gj + 1) % kStages;
+            const uint32_t ph1 = ((gj + 1) / kStages) & 1;
+            const bool more0 = j + 1 < n_t[0], more1 = j + 1 < it.n_kv;
+            ok = false;
+            if (!ks_mbar_wait(v_full + st, ph, abort, wait)) break;
+            // the first P V of an item overwrites O: the previous item's
+            // epilogue must have read it
+            if (j == 0 && r > 0 &&
+                (!ks_mbar_wait(o_empty + 0, (r - 1) & 1, abort, wait) ||
+                 !ks_mbar_wait(o_empty + 1, (r - 1) & 1, abort, wait)))
+              break;
+            // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T into the freed TMEM
+            if (j < n_t[0]) {
+              // the first half of P (keys 0-63) is read while the softmax stores the second
+              if (!ks_mbar_wait(p_half + 0, sg[0] & 1, abort, wait)) break;
+              ks_tc_fence_after();
+              issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0, 0, 4);
+              if (!ks_mbar_wait(p_full + 0, sg[0] & 1, abort, wait)) break;
+              ks_tc_fence_after();
+              issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, true, 4, 8);
+              ++sg[0];
+              if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
+            }
+            if (more1) {
+              if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
+              ks_tc_fence_after();
+            }
+            if (more0) {
+              issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
+              ks_umma_commit(s_full + 0);
+            }
+            // tile 1
+            if (!ks_mbar_wait(p_half + 1, sg[1] & 1, abort, wait)) break;
             ks_tc_fence_after();
-            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0, 0, 4);
-            if (!ks_mbar_wait(p_full + 0, j & 1, abort, wait)) break;
+            issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0, 0, 4);
+            if (!ks_mbar_wait(p_full + 1, sg[1] & 1, abort, wait)) break;
             ks_tc_fence_after();
-            issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, true, 4, 8);
-            if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
-          }
-          if (more1) {
-            if (!ks_mbar_wait(k_full + st1, ph1, abort, wait)) break;
-            ks_tc_fence_after();
-          }
-          if (more0) {
-            issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
-            ks_umma_commit(s_full + 0);
-          }
-          // tile 1
-          if (!ks_mbar_wait(p_half + 1, j & 1, abort, wait)) break;
-          ks_tc_fence_after();
-          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0, 0, 4);
-          if (!ks_mbar_wait(p_full + 1, j & 1, abort, wait)) break;
-          ks_tc_fence_after();
-          issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, true, 4, 8);
-          ks_umma_commit(kv_empty + st);
-          if (more1) {
-            issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
-            ks_umma_commit(s_full + 1);
-          } else {
-            ks_umma_commit(o_full + 1);
+            issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, true, 4, 8);
+            ++sg[1];
+            ks_umma_commit(kv_empty + st);
+            if (more1) {
+              issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
+              ks_umma_commit(s_full + 1);
+              if (j + 2 == it.n_kv) ks_umma_commit(q_empty);  // the item's last read of Q
+            } else {
+              ks_umma_commit(o_full + 1);
+            }
+            ok = true;
           }
         }
         ks_umma_commit(drain);
@@ -343,107 +405,114 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const int g = warp >> 2;         // Q tile of this warpgroup
     const int qd = warp & 3;         // TMEM lane quadrant
     const int row = qd * 32 + lane;  // row within the tile = TMEM lane
-    const int qrow = q0 + g * kTile + row;
     const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
     const uint32_t s_col = g * 128, o_col = 256 + g * 128;
-    float m = -INFINITY, l = 0.f;
+    int sg = 0;  // steps of this tile so far, over all items
     bool ok = true;
-    const int n_mine = n_t[g];
-    for (int j = 0; j < n_mine; ++j) {
-      if (!ks_mbar_wait(s_full + g, j & 1, abort, wait)) {
+    FaItem it;
+    for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+      const int qrow = it.q0 + g * kTile + row;
+      float m = -INFINITY, l = 0.f;
+      const int n_mine = g == 0 ? it.n_t0 : it.n_kv;
+      for (int j = 0; j < n_mine; ++j, ++sg) {
+        if (!ks_mbar_wait(s_full + g, sg & 1, abort, wait)) {
+          ok = false;
+          break;
+        }
+        ks_tc_fence_after();
+        uint32_t rr[128];
+        ks_tmem_ld32_at<0>(lane_addr + s_col + 0, rr);
+        ks_tmem_ld32_at<32>(lane_addr + s_col + 32, rr);
+        ks_tmem_ld32_at<64>(lane_addr + s_col + 64, rr);
+        ks_tmem_ld32_at<96>(lane_addr + s_col + 96, rr);
+        ks_tmem_wait_ld();
+        const int kv0 = j * kTile;
+        // keys beyond this row's limit are masked: causal (key > query) and length
+        int lim = nk - kv0;  // number of valid keys in this tile
+        if (causal) lim = min(lim, qrow - kv0 + 1);
+        // warp-uniform: most tiles are unmasked for all 32 rows of the warp
+        const bool full_tile = __all_sync(0xffffffffu, lim >= kTile);
+        if (!full_tile) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c >= lim) rr[c] = 0xff800000u;  // -inf
+        }
+        // row max of the raw scores (scale > 0 commutes with max), as four
+        // independent chains of 3-input max so latency does not serialise
+        float mm[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mm[u] = max3(__uint_as_float(rr[u]), __uint_as_float(rr[u + 4]), __uint_as_float(rr[u + 8]));
+#pragma unroll
+        for (int c = 12; c < 124; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mm[u] = max3(mm[u], __uint_as_float(rr[c + u]), __uint_as_float(rr[c + 4 + u]));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mm[u] = fmaxf(mm[u], __uint_as_float(rr[124 + u]));
+        const float mx = fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3]));
+        const float m_new = fmaxf(m, mx * scale_log2);
+        const bool grow = m_new > m + 8.f;  // also true on the first finite max
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O has absorbed every earlier P V of this item (the S commit
+          // follows it), rescale.
+          const float alpha = grow ? ex2(m - m_new) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+            ks_tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(lane_addr + o_col + c * 32, o);
+          }
+          ks_tmem_wait_st();
+        }
+        if (grow) {
+          l *= ex2(m - m_new);
+          m = m_new;
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
+        const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
+        // P in two halves of 64 keys (32 packed columns each), stored over S
+        // columns already in registers.  The first half is announced (p_half)
+        // once the second is computed, so the tensor core starts O += P V on
+        // keys 0-63 while the second half is stored.
+        uint32_t p[2][32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int e0 = 64 * half + 2 * c;
+            // exponent pair x = s*scale_log2 - m as one packed FFMA
+            const F2 x = fma2(F2{__uint_as_float(rr[e0]), __uint_as_float(rr[e0 + 1])}, sc2, nm2);
+            const F2 e = ((kPolyPairs >> (c & 7)) & 1u) ? exp2_poly2(x) : F2{ex2(x.x), ex2(x.y)};
+            rsum[c & 3] = add2(rsum[c & 3], e);
+            p[half][c] = ks_pack_bf16x2(e.x, e.y);
+          }
+          if (half == 0) ks_tmem_st32_at<0>(lane_addr + s_col + 0, p[0]);
+        }
+        ks_tmem_wait_st();
+        ks_tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ks_mbar_arrive(p_half + g);
+        ks_tmem_st32_at<0>(lane_addr + s_col + 32, p[1]);
+        const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
+        l += rs2.x + rs2.y;
+        ks_tmem_wait_st();
+        ks_tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ks_mbar_arrive(p_full + g);
+      }
+      // epilogue: O / l -> bf16 -> out[bh, qrow, :], then O is free again
+      if (!ok || !ks_mbar_wait(o_full + g, r & 1, abort, wait)) {
         ok = false;
         break;
       }
       ks_tc_fence_after();
-      uint32_t r[128];
-      ks_tmem_ld32_at<0>(lane_addr + s_col + 0, r);
-      ks_tmem_ld32_at<32>(lane_addr + s_col + 32, r);
-      ks_tmem_ld32_at<64>(lane_addr + s_col + 64, r);
-      ks_tmem_ld32_at<96>(lane_addr + s_col + 96, r);
-      ks_tmem_wait_ld();
-      const int kv0 = j * kTile;
-      // keys beyond this row's limit are masked: causal (key > query) and length
-      int lim = nk - kv0;  // number of valid keys in this tile
-      if (causal) lim = min(lim, qrow - kv0 + 1);
-      // warp-uniform: most tiles are unmasked for all 32 rows of the warp
-      const bool full_tile = __all_sync(0xffffffffu, lim >= kTile);
-      if (!full_tile) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= lim) r[c] = 0xff800000u;  // -inf
-      }
-      // row max of the raw scores (scale > 0 commutes with max), as four
-      // independent chains of 3-input max so latency does not serialise
-      float mm[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        mm[u] = max3(__uint_as_float(r[u]), __uint_as_float(r[u + 4]), __uint_as_float(r[u + 8]));
-#pragma unroll
-      for (int c = 12; c < 124; c += 8)
-#pragma unroll
-        for (int u = 0; u < 4; ++u) mm[u] = max3(mm[u], __uint_as_float(r[c + u]), __uint_as_float(r[c + 4 + u]));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) mm[u] = fmaxf(mm[u], __uint_as_float(r[124 + u]));
-      const float mx = fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3]));
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const bool grow = m_new > m + 8.f;  // also true on the first finite max
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O has absorbed every earlier P V (the S commit follows it), rescale.
-        const float alpha = grow ? ex2(m - m_new) : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          ks_tmem_ld32(lane_addr + o_col + c * 32, o);
-          ks_tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(lane_addr + o_col + c * 32, o);
-        }
-        ks_tmem_wait_st();
-      }
-      if (grow) {
-        l *= ex2(m - m_new);
-        m = m_new;
-      }
-      const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
-      const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
-      // P in two halves of 64 keys (32 packed columns each), stored over S
-      // columns already in registers.  The first half is announced (p_half)
-      // once the second is computed, so the tensor core starts O += P V on
-      // keys 0-63 while the second half is stored.
-      uint32_t p[2][32];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int e0 = 64 * half + 2 * c;
-          // exponent pair x = s*scale_log2 - m as one packed FFMA
-          const F2 x = fma2(F2{__uint_as_float(r[e0]), __uint_as_float(r[e0 + 1])}, sc2, nm2);
-          const F2 e = ((kPolyPairs >> (c & 7)) & 1u) ? exp2_poly2(x) : F2{ex2(x.x), ex2(x.y)};
-          rsum[c & 3] = add2(rsum[c & 3], e);
-          p[half][c] = ks_pack_bf16x2(e.x, e.y);
-        }
-        if (half == 0) ks_tmem_st32_at<0>(lane_addr + s_col + 0, p[0]);
-      }
-      ks_tmem_wait_st();
-      ks_tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ks_mbar_arrive(p_half + g);
-      ks_tmem_st32_at<0>(lane_addr + s_col + 32, p[1]);
-      const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
-      const float rs = rs2.x + rs2.y;
-      l += rs;
-      ks_tmem_wait_st();
-      ks_tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ks_mbar_arrive(p_full + g);
-    }
-    // epilogue: O / l -> bf16 -> out[bh, qrow, :]
-    if (ok && ks_mbar_wait(o_full + g, 0, abort, wait)) {
-      ks_tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t *dst = out + (int64_t(bh) * nq + qrow) * kD;
+      uint16_t *dst = out + (int64_t(it.bh) * nq + qrow) * kD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -461,6 +530,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
       }
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(o_empty + g);
     }
   }
 
@@ -916,9 +988,12 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
   cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(FaLayout::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
-  dim3 grid(unsigned((a->nq + 2 * kTile - 1) / (2 * kTile)), unsigned(bh));
+  // persistent: one CTA per SM (fewer when there are fewer work items)
+  const int64_t items = ((a->nq + 2 * kTile - 1) / (2 * kTile)) * int64_t(bh);
+  const int sms = ks::sm_count();
+  const unsigned grid = unsigned(items < sms ? items : sms);
   fa_fwd_kernel<<<grid, kThreads2, FaLayout::smem_request, st>>>(
-      tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), scale_log2, cfg->causal,
+      tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), int(bh), scale_log2, cfg->causal,
       ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }

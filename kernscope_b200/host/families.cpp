@@ -970,6 +970,10 @@ LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttenti
   LaunchGeometry g;
   g.grid_x = int((p.nq + c.tile_m - 1) / c.tile_m);
   g.grid_y = int(p.batch_heads);
+  if (c.tile_m == 256) {  // persistent: one CTA per SM over the (query block, head) items
+    g.grid_x = int(std::min<std::int64_t>(std::int64_t(g.grid_x) * g.grid_y, 148));
+    g.grid_y = 1;
+  }
   g.block_x = p.d != 128 ? 128 : c.tile_m == 256 ? 384 : 320;
   if (p.d != 128) g.grid_x = int((p.nq + 3) / 4);
   g.smem_bytes = p.d == 128 ? int(smem_bytes(c, p)) : 4 * 256 * 4;
