@@ -141,7 +141,10 @@ Clocks read_clocks(int device) {
   const std::string cmd = "nvidia-smi -i " + std::to_string(device) +
                           " --query-gpu=name,clocks.sm,clocks.mem,clocks.max.sm,power.draw,"
                           "clocks_event_reasons.active --format=csv,noheader,nounits 2>/dev/null";
-  std::unique_ptr<FILE, decltype(&pclose)> p(popen(cmd.c_str(), "r"), &pclose);
+  struct Closer {
+    void operator()(FILE *f) const { pclose(f); }
+  };
+  std::unique_ptr<FILE, Closer> p(popen(cmd.c_str(), "r"));
   if (!p) return c;
   char line[512] = {0};
   if (!std::fgets(line, sizeof(line), p.get())) return c;

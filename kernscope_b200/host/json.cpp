@@ -276,7 +276,7 @@ struct Parser {
 }  // namespace
 
 bool Value::parse(std::string_view text, Value *out, std::string *error) {
-  Parser p{text};
+  Parser p{text, 0, {}};
   Value v;
   if (!p.value(&v)) {
     if (error) *error = p.err;
