@@ -158,6 +158,9 @@ class Workload:
         self.ws = None
         if name == "reduction":
             self.ws = ops.reduction_workspace(self.sets[0][0][0], axis=-1, cfg=self.cfg)
+            # two fp64 partials, alternating by step, so that the cross-GPU
+            # combine of one step can overlap the next step's kernel
+            self.partials = [torch.empty(1, dtype=torch.float64, device=dev) for _ in range(2)]
 
     def launch(self, i, stream=None):
         ins, outs = self.sets[i % self.rotate]
@@ -169,7 +172,8 @@ class Workload:
         elif self.name == "bias_gelu":
             ops.bias_gelu(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
         elif self.name == "reduction":
-            ops.reduction(ins[0], axis=-1, out=outs[0], cfg=self.cfg, workspace=self.ws, partial_f64=outs[1],
+            ops.reduction(ins[0], axis=-1, out=outs[0], cfg=self.cfg, workspace=self.ws,
+                          partial_f64=self.partials[i % 2],
                           stream=stream)
         elif self.name.startswith("matmul"):
             ops.matmul(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
@@ -260,12 +264,40 @@ def _max_over_ranks(v, world):
     return dist.max_over_ranks(v, world, device="cuda")
 
 
-def _combine(w, world):
-    """The reduction's cross-GPU combine: all-reduce of the fp64 partial."""
+def _combine(w, world, i=0):
+    """The reduction's cross-GPU combine: all-reduce of step i's fp64 partial."""
     if world > 1 and w.name == "reduction":
         from kernscope_b200 import dist
 
-        dist.combine_partials(w.sets[0][1][1], world)
+        dist.combine_partials(w.partials[i % 2], world)
+
+
+def _reduction_steps(w, steps, world, stream):
+    """Steps of the multi-GPU reduction with each step's combine (an NCCL
+    all-reduce of its fp64 partial) on a side stream, overlapping the next
+    step's kernel; partials alternate, so step i+2's kernel waits for step
+    i's combine.  The caller's stream waits for every combine."""
+    import torch
+
+    from kernscope_b200 import dist
+
+    side = getattr(w, "_side", None) or torch.cuda.Stream()
+    w._side = side
+    done = []
+    for i in range(steps):
+        if i >= 2:
+            stream.wait_event(done[i - 2])
+        w.launch(i)
+        k = torch.cuda.Event()
+        k.record(stream)
+        side.wait_event(k)
+        with torch.cuda.stream(side):
+            dist.combine_partials(w.partials[i % 2], world)
+        c = torch.cuda.Event()
+        c.record(side)
+        done.append(c)
+    for c in done[-2:]:
+        stream.wait_event(c)
 
 
 def measure_device(w, steps, warmup, world, graph=True):
@@ -275,9 +307,12 @@ def measure_device(w, steps, warmup, world, graph=True):
     import torch
 
     stream = torch.cuda.current_stream()
-    for i in range(warmup):
-        w.launch(i)
-        _combine(w, world)
+    overlap = world > 1 and w.name == "reduction"
+    if overlap:
+        _reduction_steps(w, warmup, world, stream)
+    else:
+        for i in range(warmup):
+            w.launch(i)
     torch.cuda.synchronize()
     g = None
     per_graph = w.rotate if w.rotate > 1 else 1
@@ -306,10 +341,11 @@ def measure_device(w, steps, warmup, world, graph=True):
             g.replay()
         for i in range(rem):
             w.launch(i)
+    elif overlap:
+        _reduction_steps(w, steps, world, stream)
     else:
         for i in range(steps):
             w.launch(i)
-            _combine(w, world)
     e1.record(stream)
     e1.synchronize()
     ms = e0.elapsed_time(e1)
@@ -658,7 +694,9 @@ def main():
                        "shape_per_gpu": list(spec["shape"]), "kernel": kernel,
                        "parallelism": f"dp{world} (weak: one batch per GPU)",
                        "l2": "rotating input/output sets, working set >= 4x L2 (no step reads inputs from L2)",
-                       "timing": "CUDA events on the launching stream, graph-replayed launch loop, max over ranks"},
+                       "timing": "CUDA events on the launching stream, graph-replayed launch loop (multi-GPU "
+                                 "reduction: launches with each step's NCCL combine overlapping the next "
+                                 "step), max over ranks"},
             "roofline": {"bound": spec["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": peaks["source"]},
