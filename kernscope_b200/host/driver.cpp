@@ -10,7 +10,9 @@
 #include <fstream>
 #include <map>
 #include <memory>
+#include <set>
 #include <sstream>
+#include <tuple>
 
 #include "bench.h"
 #include "families.h"
@@ -836,6 +838,29 @@ int ks_tune_query_json(const char *request_json, char *out, size_t cap, size_t *
     }
     res = object({{"saved", Value(saved)}, {"records", Value(std::move(recs))}, {"warnings", Value(int(w.size()))},
                   {"best", best}});
+  } else if (op == "db_load") {
+    // Loads one JSONL db and answers query_best for every workload key in it,
+    // in first-seen order.
+    db::Database d;
+    std::vector<db::LoadWarning> w;
+    const bool opened = d.load(j.string_or("path", ""), w);
+    std::vector<Value> warn, best;
+    for (const auto &lw : w) warn.push_back(Value(lw.message));
+    std::set<std::tuple<std::string, std::string, std::string>> seen;
+    for (const auto &r : d.records()) {
+      if (!seen.insert({r.gpu_arch, r.kernel_family, r.shape_hash}).second) continue;
+      if (auto b = d.query_best(r.gpu_arch, r.kernel_family, r.shape_hash))
+        best.push_back(object({{"gpu_arch", Value(b->gpu_arch)}, {"kernel_family", Value(b->kernel_family)},
+                               {"shape_hash", Value(b->shape_hash)}, {"config", b->config},
+                               {"median", Value(b->timings.median)}}));
+    }
+    res = object({{"opened", Value(opened)}, {"records", Value(int(d.size()))}, {"warnings", Value(std::move(warn))},
+                  {"best", Value(std::move(best))}});
+  } else if (op == "quantile") {
+    std::vector<double> s;
+    if (const Value *v = j.find("samples"); v && v->is_array())
+      for (const Value &x : v->as_array()) s.push_back(x.as_number());
+    res = object({{"q", Value(bench::quantile(std::move(s), j.number_or("q", 0.5)))}});
   } else {
     return write_out(object({{"error", Value("unknown op '" + op + "'")}}).dump(), out, cap, needed) == 0 ? 2 : -1;
   }

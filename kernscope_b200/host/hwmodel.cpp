@@ -46,7 +46,7 @@ namespace occupancy {
 const char *limiter_name(Limiter l) noexcept {
   switch (l) {
     case Limiter::kRegisters: return "registers";
-    case Limiter::kSharedMemory: return "shared_memory";
+    case Limiter::kSharedMemory: return "shared";  // the reference's contract string (libs/occupancy/src/occupancy.cpp:50-62)
     case Limiter::kThreads: return "threads";
     case Limiter::kBlocks: return "blocks";
     case Limiter::kTmem: return "tmem";
@@ -72,12 +72,16 @@ OccupancyResult compute_occupancy(const ArchInfo &a, int regs, int smem, int blo
   };
   Cand c[5];
   int n = 0;
+  // Candidates in tie-break order: on equal counts the earlier one is named
+  // (registers > shared > threads > blocks, the reference's priority in
+  // libs/occupancy/src/occupancy.cpp:69-93; TMEM, which it does not model,
+  // last). Zero shared memory or TMEM is "not requested" and never limits.
   const int regs_rounded = ((std::max(regs, 1) + a.reg_granule - 1) / a.reg_granule) * a.reg_granule;
   c[n++] = {a.regs_per_sm / (regs_rounded * a.warp_size * warps), Limiter::kRegisters};
-  c[n++] = {smem > 0 ? a.smem_per_sm_bytes / smem : a.max_blocks_per_sm, Limiter::kSharedMemory};
+  if (smem > 0) c[n++] = {a.smem_per_sm_bytes / smem, Limiter::kSharedMemory};
   c[n++] = {a.max_threads_per_sm / (warps * a.warp_size), Limiter::kThreads};
   c[n++] = {a.max_blocks_per_sm, Limiter::kBlocks};
-  c[n++] = {tmem_cols > 0 ? a.tmem_columns_per_sm / tmem_cols : a.max_blocks_per_sm, Limiter::kTmem};
+  if (tmem_cols > 0) c[n++] = {a.tmem_columns_per_sm / tmem_cols, Limiter::kTmem};
   Cand best = c[0];
   for (int i = 1; i < n; ++i)
     if (c[i].blocks < best.blocks) best = c[i];
@@ -148,12 +152,18 @@ std::int64_t compute_bytes_moved(KernelFamily f, const Shape &s) noexcept {
 
 std::int64_t reference_model_bytes(KernelFamily f, const Shape &s) noexcept {
   const std::int64_t b = s.dtype_bytes;
+  // The reference's element model (libs/roofline/src/roofline.cpp:66-82):
+  // parameter vectors and the reduction's output are not counted.
   switch (f) {
+    case KernelFamily::kGemm: return compute_bytes_moved(f, s);
     case KernelFamily::kFusedBiasGelu: return 3 * s.n * b;  // x, bias (per element), y
+    case KernelFamily::kSoftmax:
+    case KernelFamily::kLayerNorm: return 2 * s.n * b;
+    case KernelFamily::kReduction: return s.n * b;
     case KernelFamily::kFlashAttention:                     // standard attention: s(4Nd + 4N^2)
       return std::max<std::int64_t>(s.m, 1) * b * (4 * s.n * s.d + 4 * s.n * s.n);
-    default: return compute_bytes_moved(f, s);
   }
+  return 0;
 }
 
 double arithmetic_intensity(KernelFamily f, const Shape &s) noexcept {
