@@ -569,8 +569,39 @@ def main_reference(args):
                                        "(numpy restatement of tests/golden/kernscope_golden/refs.py, 1 BLAS "
                                        "thread per process)"},
             "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    gk = _reference_gpu_kernels()
+    if gk is not None:
+        line["reference_gpu_kernels"] = gk
     print(json.dumps(line))
     return 0
+
+
+def _reference_gpu_kernels():
+    """The reference generator's own kernels (its tuner's auto grid, built by
+    oracle/ref_tune/build_ref_kernels.py) timed on this GPU at the benchmark
+    shapes, best gate-passing config per family; None without a GPU or
+    without the built kernels.  Informational: the arm's value stays the
+    reference's CPU path."""
+    try:
+        import torch
+
+        if not torch.cuda.is_available():
+            return None
+        from oracle import ref_gpu
+
+        if ref_gpu.index() is None:
+            return None
+        torch.cuda.set_device(0)
+        out = {}
+        for fam in ref_gpu.FAMILIES:
+            try:
+                out[fam] = ref_gpu.run_family(fam)
+            except Exception as exc:  # noqa: BLE001 - one family's failure is reported, not fatal
+                out[fam] = {"unavailable": str(exc)[:200]}
+            torch.cuda.empty_cache()
+        return out
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": str(exc)[:200]}
 
 
 def _ref_chunk(job):

@@ -15,12 +15,18 @@
 //   occupancy <arch> regs smem block   compute_occupancy
 //                                      (libs/occupancy/include/kernscope/occupancy.h:85-87)
 //   quantile <q> <s0,s1,...>           bench::quantile (libs/bench/include/kernscope/bench.h:105)
+//   gen <family> <arch> <shape> <out.cu|-> key=value...
+//                                      validate_config + launch_geometry +
+//                                      kernel_symbol + generate_to_file of the
+//                                      family's generator (tools/tune/include/
+//                                      kernscope/tune/*_gen.h); "-" skips the file
 #include "kernscope/arch.h"
 #include "kernscope/bench.h"
 #include "kernscope/db.h"
 #include "kernscope/occupancy.h"
 #include "kernscope/roofline.h"
 #include "kernscope/tune/driver.h"
+#include "ref_gen.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -47,7 +53,7 @@ int usage() {
   std::fprintf(stderr,
                "usage: ref_tune_check hash <family> <dims> [arch] | db <path> | "
                "roofline <family> m n k d dtype_bytes | occupancy <arch> regs smem block | "
-               "quantile <q> <samples>\n");
+               "quantile <q> <samples> | gen <family> <arch> <shape> <out|-> key=value...\n");
   return 2;
 }
 
@@ -142,6 +148,38 @@ int cmd_quantile(int argc, char **argv) {
   return 0;
 }
 
+int cmd_gen(int argc, char **argv) {
+  if (argc < 6) return usage();
+  const std::string family = argv[2], arch = argv[3], out = std::string(argv[5]) == "-" ? "" : argv[5];
+  std::vector<std::int64_t> shape;
+  for (const auto &t : split(argv[4], ',')) shape.push_back(std::strtoll(t.c_str(), nullptr, 10));
+  RefCfg cfg;
+  for (int i = 6; i < argc; ++i) {
+    const std::string kv = argv[i];
+    const auto eq = kv.find('=');
+    if (eq == std::string::npos) return usage();
+    cfg[kv.substr(0, eq)] = kv.substr(eq + 1);
+  }
+  RefGen g;
+  std::string err;
+  bool ok;
+  if (family == "matmul") ok = ref_gen_matmul(arch, shape, cfg, out, &g, &err);
+  else if (family == "flash_attention") ok = ref_gen_flash(arch, shape, cfg, out, &g, &err);
+  else ok = ref_gen_elem(family, arch, shape, cfg, out, &g, &err);
+  if (!ok) {
+    std::fprintf(stderr, "ref_tune_check gen: %s\n", err.c_str());
+    return 1;
+  }
+  const json::Value v = json::object({{"valid", json::Value(g.valid)},
+                                      {"reason", json::Value(g.reason)},
+                                      {"symbol", json::Value(g.symbol)},
+                                      {"grid", json::array({json::Value(g.grid_x), json::Value(g.grid_y)})},
+                                      {"block", json::array({json::Value(g.block_x), json::Value(g.block_y)})},
+                                      {"smem_bytes", json::Value(static_cast<double>(g.smem_bytes))}});
+  std::printf("%s\n", v.dump().c_str());
+  return 0;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
@@ -152,5 +190,6 @@ int main(int argc, char **argv) {
   if (cmd == "roofline") return cmd_roofline(argc, argv);
   if (cmd == "occupancy") return cmd_occupancy(argc, argv);
   if (cmd == "quantile") return cmd_quantile(argc, argv);
+  if (cmd == "gen") return cmd_gen(argc, argv);
   return usage();
 }
