@@ -113,33 +113,6 @@ KS_DEV F2 add2(F2 a, F2 b) {
   return d;
 }
 
-// One pair in eight of each P row (c % 8 == 0) is exponentiated on the FMA
-// pipe instead of the ex2 unit (16 per SM per clock), which both softmax
-// warpgroups share.  Measured at C5: +6 % causal, unchanged non-causal; a
-// quarter or more is slower (the extra FMA-pipe instructions cost more issue
-// slots than the ex2 unit saves).
-constexpr uint32_t kPolyPairs = 0x01u;
-
-// 2^x for a pair on the FMA pipe, for x <= 64: x = n + f with n the nearest
-// integer (adding 1.5 * 2^23 rounds x into the low mantissa bits) and f in
-// [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted for the least maximum
-// relative error on that interval (7.5e-5, below bf16's 2^-9); n is added to
-// the exponent field.  Inputs are clamped at -125 (a masked key then gives
-// 2^-125 instead of 0, negligible against a row sum >= 1).
-KS_DEV F2 exp2_poly2(F2 x) {
-  x.x = fmaxf(x.x, -125.f);
-  x.y = fmaxf(x.y, -125.f);
-  const F2 t = add2(x, F2{12582912.f, 12582912.f});
-  const F2 n = add2(t, F2{-12582912.f, -12582912.f});
-  const F2 f = fma2(n, F2{-1.f, -1.f}, x);
-  F2 q = fma2(F2{0.05517134f, 0.05517134f}, f, F2{0.24261034f, 0.24261034f});
-  q = fma2(q, f, F2{0.69326097f, 0.69326097f});
-  q = fma2(q, f, F2{0.99992812f, 0.99992812f});
-  // (bits(t) << 23) == n << 23 modulo 2^32: the low bits of bits(t) hold n
-  return F2{__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
-            __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23))};
-}
-
 KS_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -487,7 +460,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             const int e0 = 64 * half + 2 * c;
             // exponent pair x = s*scale_log2 - m as one packed FFMA
             const F2 x = fma2(F2{__uint_as_float(rr[e0]), __uint_as_float(rr[e0 + 1])}, sc2, nm2);
-            const F2 e = ((kPolyPairs >> (c & 7)) & 1u) ? exp2_poly2(x) : F2{ex2(x.x), ex2(x.y)};
+            const F2 e{ex2(x.x), ex2(x.y)};
             rsum[c & 3] = add2(rsum[c & 3], e);
             p[half][c] = ks_pack_bf16x2(e.x, e.y);
           }
