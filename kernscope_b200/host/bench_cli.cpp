@@ -29,6 +29,7 @@
 #include <cstring>
 #include <filesystem>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -260,7 +261,7 @@ int measure_compute(void *sink, const char *family, const char *label, const cha
 
 }  // namespace
 
-int main(int argc, char **argv) {
+static int run_main(int argc, char **argv) {
   Args a;
   int rc = 0;
   if (!parse(argc, argv, &a, &rc)) return rc;
@@ -333,7 +334,11 @@ int main(int argc, char **argv) {
     rec.provenance.timestamp = ts;
     rec.provenance.tool_version = kToolVersion;
     rec.provenance.mode = "measured";
-    db.put(std::move(rec));
+    try {
+      db.put(std::move(rec));
+    } catch (const std::invalid_argument &e) {
+      std::fprintf(stderr, "kernscope-bench: record not stored: %s\n", e.what());
+    }
   }
   std::error_code ec;
   const std::filesystem::path dbp(a.db);
@@ -378,4 +383,17 @@ int main(int argc, char **argv) {
                 saved ? (", db " + a.db).c_str() : ", db not written");
   }
   return floors_ok ? 0 : 1;
+}
+
+// An exception from the library ends the tool with an error status and its
+// message instead of std::terminate.
+int main(int argc, char **argv) {
+  try {
+    return run_main(argc, argv);
+  } catch (const std::exception &e) {
+    std::fprintf(stderr, "kernscope-bench: internal error: %s\n", e.what());
+  } catch (...) {
+    std::fprintf(stderr, "kernscope-bench: internal error\n");
+  }
+  return 2;
 }

@@ -467,8 +467,12 @@ DriverResult tune(const DriverOptions &opts, const DriverHooks *hooks) {
       r.config = v.config;
       r.timings = {v.median, v.p20, v.p80};
       r.provenance = {db::utc_timestamp(), kToolVersion, "measured"};
-      d.put(std::move(r));
-      ++db_records;
+      try {
+        d.put(std::move(r));
+        ++db_records;
+      } catch (const std::invalid_argument &) {
+        // non-finite timings: the variant's evidence keeps them, the db does not
+      }
     }
     db_ok = d.save(opts.db_path);
   }
@@ -697,15 +701,30 @@ kernscope::tune::DriverOptions options_from(const Value &j) {
   o.seed = std::uint64_t(j.number_or("seed", 0));
   return o;
 }
-}  // namespace
 
-extern "C" {
+// Exceptions never cross the C ABI: report them as an internal error.
+template <class F>
+int guarded(char *out, size_t cap, size_t *needed, F &&f) {
+  try {
+    return f();
+  } catch (const std::exception &e) {
+    return write_out(kernscope::db::json::object({{"status", Value("internal_error")}, {"error", Value(e.what())}})
+                         .dump(),
+                     out, cap, needed) == 0
+               ? 2
+               : -1;
+  } catch (...) {
+    return write_out("{\"status\":\"internal_error\",\"error\":\"unknown exception\"}", out, cap, needed) == 0
+               ? 2
+               : -1;
+  }
+}
 
 // Run the tuning pipeline: options as JSON (keys of DriverOptions plus
 // "inject_gate_failure": config index whose gate output is zeroed); writes
 // the evidence JSON.  Returns the CLI exit code (0 ok, 1 no viable config,
 // 2 otherwise) or -1 when `out` is too small (*needed = bytes required).
-int ks_tune_run_json(const char *options_json, char *out, size_t cap, size_t *needed) {
+int tune_run_json(const char *options_json, char *out, size_t cap, size_t *needed) {
   Value j;
   std::string err;
   if (!options_json || !Value::parse(options_json, &j, &err)) {
@@ -736,7 +755,7 @@ int ks_tune_run_json(const char *options_json, char *out, size_t cap, size_t *ne
 //   enumerate {family, shape, full, causal?, gelu?}; validate {family, shape, config};
 //   occupancy {regs, smem, block, tmem}; roofline {family, shape, causal?};
 //   geometry {family, shape, config}; peaks {}; db_roundtrip {path, records[]}
-int ks_tune_query_json(const char *request_json, char *out, size_t cap, size_t *needed) {
+int tune_query_json(const char *request_json, char *out, size_t cap, size_t *needed) {
   using namespace kernscope;
   using kernscope::db::json::object;
   Value j;
@@ -821,7 +840,12 @@ int ks_tune_query_json(const char *request_json, char *out, size_t cap, size_t *
     if (const Value *rs = j.find("records"); rs && rs->is_array())
       for (const Value &rv : rs->as_array()) {
         db::Record rec;
-        if (db::record_from_json(rv, &rec, &err)) d.put(std::move(rec));
+        if (db::record_from_json(rv, &rec, &err)) {
+          try {
+            d.put(std::move(rec));
+          } catch (const std::invalid_argument &) {
+          }
+        }
       }
     const std::string path = j.string_or("path", "");
     const bool saved = d.save(path);
@@ -867,4 +891,17 @@ int ks_tune_query_json(const char *request_json, char *out, size_t cap, size_t *
   return write_out(object({{"result", res}}).dump(), out, cap, needed) == 0 ? 0 : -1;
 }
 
+}  // namespace
+
+extern "C" {
+
+int ks_tune_run_json(const char *options_json, char *out, size_t cap, size_t *needed) {
+  return guarded(out, cap, needed, [&] { return tune_run_json(options_json, out, cap, needed); });
+}
+
+int ks_tune_query_json(const char *request_json, char *out, size_t cap, size_t *needed) {
+  return guarded(out, cap, needed, [&] { return tune_query_json(request_json, out, cap, needed); });
+}
+
 }  // extern "C"
+

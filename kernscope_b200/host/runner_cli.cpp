@@ -26,6 +26,7 @@
 // usage error.  No silent skips.
 #include <cstdint>
 #include <cstdio>
+#include <exception>
 #include <cstdlib>
 #include <fstream>
 #include <iterator>
@@ -115,7 +116,7 @@ bool tuner_view(const Options &o, std::string *fam, std::vector<std::int64_t> *s
 
 }  // namespace
 
-int main(int argc, char **argv) {
+static int run_main(int argc, char **argv) {
   Options o;
   for (int a = 1; a < argc; ++a) {
     const std::string s = argv[a];
@@ -246,4 +247,17 @@ int main(int argc, char **argv) {
   std::printf("ran %s (%s) -> %s (%zu bytes)\n", fam->symbol(cfg).c_str(), cfg.dump().c_str(), o.out.c_str(),
               o.out_size);
   return 0;
+}
+
+// An exception from the library ends the tool with an error status and its
+// message instead of std::terminate.
+int main(int argc, char **argv) {
+  try {
+    return run_main(argc, argv);
+  } catch (const std::exception &e) {
+    std::fprintf(stderr, "ks-template-runner: internal error: %s\n", e.what());
+  } catch (...) {
+    std::fprintf(stderr, "ks-template-runner: internal error\n");
+  }
+  return 1;
 }

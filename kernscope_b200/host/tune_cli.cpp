@@ -6,6 +6,7 @@
 // sm_100a).  The LLVM verifier gate (--verify / --inject-risky) is not part
 // of this build: those flags are reported as unsupported (exit 2).
 #include <cstdio>
+#include <exception>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -86,7 +87,7 @@ void print_html(const kernscope::db::json::Value &ev) {
 
 }  // namespace
 
-int main(int argc, char **argv) {
+static int run_main(int argc, char **argv) {
   kernscope::tune::DriverOptions o;
   std::string mode = "json", repro, shape_s;
   bool have_kernel = false, have_shape = false;
@@ -197,4 +198,17 @@ int main(int argc, char **argv) {
     case kernscope::tune::DriverStatus::kNoViableConfig: return 1;
     default: return 2;
   }
+}
+
+// An exception from the library ends the tool with an error status and its
+// message instead of std::terminate.
+int main(int argc, char **argv) {
+  try {
+    return run_main(argc, argv);
+  } catch (const std::exception &e) {
+    std::fprintf(stderr, "kernscope-tune: internal error: %s\n", e.what());
+  } catch (...) {
+    std::fprintf(stderr, "kernscope-tune: internal error\n");
+  }
+  return 2;
 }

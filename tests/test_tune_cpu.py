@@ -149,3 +149,12 @@ def test_reproducer_source_mentions_config():
     assert g["grid_x"] == 148 and g["block_x"] == 192 and g["tmem_columns"] == 512
     assert "ks_matmul_launch" in g["source"] and "{128, 256, 64, 4, 2, 8}" in g["source"]
     assert g["gate_shape"] == [64, 64, 64]
+
+
+def test_exceptions_do_not_cross_the_c_abi():
+    """A library exception (here get_arch's unknown-arch error) becomes an
+    error status of the C entry point, not a terminated process."""
+    with pytest.raises(ValueError, match="unknown arch"):
+        tune.query("occupancy", arch="gfx9999", regs=32, smem=0, block=128)
+    rc, ev = tune.run(kernel_family="softmax", shape=[64, 1024], arch="gfx9999", live_bench=False)
+    assert rc == 2 and "unknown arch" in ev.get("message", "") + ev.get("error", "")
