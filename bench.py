@@ -377,7 +377,7 @@ def measure_e2e(w, steps, world):
 
     if w.name in ("softmax", "layernorm", "bias_gelu"):
         rows = ins[0].shape[0]
-        pipe = ops.HostRowPipeline(rows, chunk_rows=max(1, rows // 8))
+        pipe = ops.HostRowPipeline(rows)
         row_in = [0]  # x is row-sharded; gamma/beta/bias stay whole
         h2d_whole = [(h, t) for k, (h, t) in enumerate(zip(host_in, ins)) if k not in row_in]
 
