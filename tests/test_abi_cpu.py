@@ -81,3 +81,33 @@ def test_launch_without_gpu_reports_error(N):
     cfg = N.SoftmaxConfig(256, 8, 0)
     args = N.SoftmaxArgs(None, None, 4, 64)
     assert N.lib.ks_softmax_launch(C.byref(cfg), C.byref(args), None) == N.KS_ERR_INVALID_ARGS
+
+
+def _launch_cases(N):
+    """(entry point, config, args) with every pointer null, per family."""
+    return [
+        ("ks_softmax_launch", N.SoftmaxConfig(256, 8, 0), N.SoftmaxArgs(None, None, 64, 64)),
+        ("ks_layernorm_launch", N.LayerNormConfig(128, 8, 0), N.LayerNormArgs(None, None, None, None, 64, 64, 1e-5)),
+        ("ks_bias_gelu_launch", N.BiasGeluConfig(128, 8, 1), N.BiasGeluArgs(None, None, None, 64 * 64, 64)),
+        ("ks_reduction_launch", N.ReductionConfig(256, 4, 2),
+         N.ReductionArgs(None, None, 64, 64, 0, 0, 0, None, 0, None)),
+        ("ks_matmul_launch", N.MatmulConfig(128, 256, 64, 4, 2, 16), N.MatmulArgs(None, None, None, 64, 64, 64)),
+        ("ks_flash_attention_launch", N.FlashAttentionConfig(256, 128, 2, 1),
+         N.FlashAttentionArgs(None, None, None, None, 1, 1, 128, 128, 128, 0.0)),
+    ]
+
+
+def test_every_launch_rejects_null_pointers_and_null_structs(N):
+    """Each family's launch checks its arguments before any CUDA call: null
+    device pointers give invalid_args, and so do null config/args structs."""
+    for fn, cfg, args in _launch_cases(N):
+        f = getattr(N.lib, fn)
+        assert f(C.byref(cfg), C.byref(args), None) == N.KS_ERR_INVALID_ARGS, fn
+        assert f(None, C.byref(args), None) == N.KS_ERR_INVALID_ARGS, fn
+        assert f(C.byref(cfg), None, None) == N.KS_ERR_INVALID_ARGS, fn
+
+
+def test_negative_sizes_are_rejected(N):
+    args = N.SoftmaxArgs(0x1000, 0x2000, -1, 64)
+    assert N.lib.ks_softmax_launch(C.byref(N.SoftmaxConfig(256, 8, 0)), C.byref(args), None) == N.KS_ERR_INVALID_ARGS
+    assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 16), -1, 64, 64)[0] != N.KS_OK
