@@ -221,8 +221,9 @@ int ks_matmul_launch(const ks_matmul_config *cfg, const ks_matmul_args *args, vo
  * K/V [B,H,Nk,d], O [B,H,Nq,d], bf16, fp32 online-softmax statistics.
  * batch = heads = 1 is the reference's single-head ABI (q, k, v, out, nq,
  * nk, d).  scale <= 0 selects 1/sqrt(d).  causal masks col > row (the
- * reference's gj > gi test).  d in 1..256: tensor cores at d = 128, CUDA cores
- * otherwise; Nq, Nk any positive value.                                     */
+ * reference's gj > gi test).  d in 1..256: tensor cores at d = 128 (either
+ * tile_m) and d = 64 (tile_m 256), CUDA cores otherwise; Nq, Nk any positive
+ * value.                                                                    */
 typedef struct ks_flash_attention_config {
   int tile_m; int tile_n; int stages; int causal;
 } ks_flash_attention_config;

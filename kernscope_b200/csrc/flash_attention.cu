@@ -63,11 +63,19 @@ constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
 constexpr int kStages = 2;
 
 
+// Bytes of one [128 rows x D] bf16 tile: D / 64 boxes of 64 columns.
+template <int D>
+constexpr uint32_t tile_bytes() {
+  return uint32_t(D / 64) * kBox;
+}
+
+template <int D>
 struct FaLayout {
-  static constexpr uint32_t q_off = 0;                           // Q0, Q1
-  static constexpr uint32_t k_off = q_off + 2 * kTileBytes;      // K[stages]
-  static constexpr uint32_t v_off = k_off + kStages * kTileBytes;  // V[stages]
-  static constexpr uint32_t bar_off = v_off + kStages * kTileBytes;
+  static constexpr uint32_t kTB = tile_bytes<D>();
+  static constexpr uint32_t q_off = 0;                      // Q0, Q1
+  static constexpr uint32_t k_off = q_off + 2 * kTB;        // K[stages]
+  static constexpr uint32_t v_off = k_off + kStages * kTB;  // V[stages]
+  static constexpr uint32_t bar_off = v_off + kStages * kTB;
   // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain, p_half[2],
   // o_empty[2], q_empty
   static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1 + 2 + 2 + 1;
@@ -128,10 +136,11 @@ KS_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 // S(tile g) = Q_g K_j^T: M=128, N=128 (keys), K=d=128 in 8 steps of 16.
 // Q and K tiles are K-major: two 64-column boxes of 128 rows (16 KB apart),
 // 128-byte rows, 8-row groups 1024 bytes apart.
+template <int D = kD>
 KS_DEV void issue_s(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
   constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, false);
 #pragma unroll
-  for (int kk = 0; kk < kD / 16; ++kk) {
+  for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
     ks_umma_ss(d_tmem, ks_umma_desc_sw128(q_addr + off, 16, 1024), ks_umma_desc_sw128(k_addr + off, 16, 1024),
                idesc, kk > 0);
@@ -142,9 +151,10 @@ KS_DEV void issue_s(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
 // P comes from TMEM (8 columns = 16 bf16 per step); V is MN-major: two
 // 64-column boxes 16 KB apart (LBO), 8 key-rows 1024 bytes apart (SBO),
 // 16 key-rows = 2048 bytes per step.
+template <int D = kD>
 KS_DEV void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate, int kk0 = 0,
                      int kk1 = kTile / 16) {
-  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 128, false, true);
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, D, false, true);
 #pragma unroll
   for (int kk = kk0; kk < kk1; ++kk)
     ks_umma_ts(o_tmem, p_tmem + kk * 8, ks_umma_desc_sw128(v_addr + kk * 2048, kBox, 1024), idesc,
@@ -185,11 +195,13 @@ KS_DEV bool fa_item(int r, int c, int G, int num_items, int num_qb, int n_bh, in
 // Persistent: one CTA per SM walks its work items; the next item's Q load
 // and first QK^T MMAs run while the softmax warpgroups finish the current
 // item's epilogue.  Phases of the per-step barriers continue across items.
+template <int D>
 __global__ void __launch_bounds__(kThreads2, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
                   int n_bh, float scale_log2, int causal, KsWait wait) {
-  using L = FaLayout;
+  using L = FaLayout<D>;
+  constexpr uint32_t kTB = L::kTB;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -259,10 +271,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
         for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
           // the previous item's last QK^T MMA has read Q
           if (r > 0 && !ks_mbar_wait(q_empty, (r - 1) & 1, abort, wait)) break;
-          ks_mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+          ks_mbar_arrive_expect_tx(q_full, 2 * kTB);
           for (int g = 0; g < 2; ++g)
-            for (int h = 0; h < 2; ++h)
-              ks_tma_load_3d(qs + g * kTileBytes + h * kBox, &tm_q, q_full, h * 64, it.q0 + g * kTile, it.bh);
+            for (int h = 0; h < D / 64; ++h)
+              ks_tma_load_3d(qs + g * kTB + h * kBox, &tm_q, q_full, h * 64, it.q0 + g * kTile, it.bh);
           ++q_loads;
           for (int j = 0; j < it.n_kv; ++j, ++gj) {
             const int st = gj % kStages;
@@ -271,13 +283,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
               ok = false;
               break;
             }
-            uint8_t *ks = smem + L::k_off + st * kTileBytes;
-            uint8_t *vs = smem + L::v_off + st * kTileBytes;
-            ks_mbar_arrive_expect_tx(k_full + st, kTileBytes);
-            for (int h = 0; h < 2; ++h)
+            uint8_t *ks = smem + L::k_off + st * kTB;
+            uint8_t *vs = smem + L::v_off + st * kTB;
+            ks_mbar_arrive_expect_tx(k_full + st, kTB);
+            for (int h = 0; h < D / 64; ++h)
               ks_tma_load_3d(ks + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, it.bh);
-            ks_mbar_arrive_expect_tx(v_full + st, kTileBytes);
-            for (int h = 0; h < 2; ++h)
+            ks_mbar_arrive_expect_tx(v_full + st, kTB);
+            for (int h = 0; h < D / 64; ++h)
               ks_tma_load_3d(vs + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, it.bh);
             armed |= 1u << st;
             armed_par = (armed_par & ~(1u << st)) | (ph << st);
@@ -310,9 +322,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
               !ks_mbar_wait(k_full + gj % kStages, (gj / kStages) & 1, abort, wait))
             break;
           ks_tc_fence_after();
-          issue_s(t_s[0], q_addr, k_addr + (gj % kStages) * kTileBytes);
+          issue_s<D>(t_s[0], q_addr, k_addr + (gj % kStages) * kTB);
           ks_umma_commit(s_full + 0);
-          issue_s(t_s[1], q_addr + kTileBytes, k_addr + (gj % kStages) * kTileBytes);
+          issue_s<D>(t_s[1], q_addr + kTB, k_addr + (gj % kStages) * kTB);
           ks_umma_commit(s_full + 1);
           if (it.n_kv == 1) ks_umma_commit(q_empty);  // that was the item's last read of Q
           for (int j = 0; j < it.n_kv && ok; ++j, ++gj) {
@@ -334,10 +346,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
               // the first half of P (keys 0-63) is read while the softmax stores the second
               if (!ks_mbar_wait(p_half + 0, sg[0] & 1, abort, wait)) break;
               ks_tc_fence_after();
-              issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, j > 0, 0, 4);
+              issue_pv<D>(t_o[0], t_s[0], v_addr + st * kTB, j > 0, 0, 4);
               if (!ks_mbar_wait(p_full + 0, sg[0] & 1, abort, wait)) break;
               ks_tc_fence_after();
-              issue_pv(t_o[0], t_s[0], v_addr + st * kTileBytes, true, 4, 8);
+              issue_pv<D>(t_o[0], t_s[0], v_addr + st * kTB, true, 4, 8);
               ++sg[0];
               if (j + 1 == n_t[0]) ks_umma_commit(o_full + 0);
             }
@@ -346,20 +358,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
               ks_tc_fence_after();
             }
             if (more0) {
-              issue_s(t_s[0], q_addr, k_addr + st1 * kTileBytes);
+              issue_s<D>(t_s[0], q_addr, k_addr + st1 * kTB);
               ks_umma_commit(s_full + 0);
             }
             // tile 1
             if (!ks_mbar_wait(p_half + 1, sg[1] & 1, abort, wait)) break;
             ks_tc_fence_after();
-            issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, j > 0, 0, 4);
+            issue_pv<D>(t_o[1], t_s[1], v_addr + st * kTB, j > 0, 0, 4);
             if (!ks_mbar_wait(p_full + 1, sg[1] & 1, abort, wait)) break;
             ks_tc_fence_after();
-            issue_pv(t_o[1], t_s[1], v_addr + st * kTileBytes, true, 4, 8);
+            issue_pv<D>(t_o[1], t_s[1], v_addr + st * kTB, true, 4, 8);
             ++sg[1];
             ks_umma_commit(kv_empty + st);
             if (more1) {
-              issue_s(t_s[1], q_addr + kTileBytes, k_addr + st1 * kTileBytes);
+              issue_s<D>(t_s[1], q_addr + kTB, k_addr + st1 * kTB);
               ks_umma_commit(s_full + 1);
               if (j + 2 == it.n_kv) ks_umma_commit(q_empty);  // the item's last read of Q
             } else {
@@ -431,7 +443,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           // follows it), rescale.
           const float alpha = grow ? ex2(m - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
             ks_tmem_ld32(lane_addr + o_col + c * 32, o);
             ks_tmem_wait_ld();
@@ -485,9 +497,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       }
       ks_tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t *dst = out + (int64_t(it.bh) * nq + qrow) * kD;
+      uint16_t *dst = out + (int64_t(it.bh) * nq + qrow) * D;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         ks_tmem_ld32(lane_addr + o_col + c * 32, o);
         ks_tmem_wait_ld();
@@ -881,6 +893,17 @@ __global__ void __launch_bounds__(128) fa_simt_kernel(const uint16_t *__restrict
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <int D>
+int launch_fwd(unsigned grid, cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+               const ks_flash_attention_args &a, uint64_t bh, float scale_log2, int causal) {
+  cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(FaLayout<D>::smem_request));
+  if (e != cudaSuccess) return ks::map_cuda(e);
+  fa_fwd_kernel<D><<<grid, kThreads2, FaLayout<D>::smem_request, st>>>(
+      tq, tk, tv, static_cast<uint16_t *>(a.out), int(a.nq), int(a.nk), int(bh), scale_log2, causal, ks::wait_ctx());
+  return ks::map_cuda(cudaGetLastError());
+}
+
 }  // namespace
 
 extern "C" {
@@ -903,7 +926,7 @@ int ks_flash_attention_validate(const ks_flash_attention_config *cfg, const ks_f
     return KS_ERR_INVALID_CONFIG;
   }
   if (a->d < 1 || a->d > kSimtMaxD) {
-    ks::set_reason(reason, len, "flash_attention: head dim %lld unsupported (1..256; tensor cores at d = 128)",
+    ks::set_reason(reason, len, "flash_attention: head dim %lld unsupported (1..256; tensor cores at d = 128, and at d = 64 with tile_m 256)",
                    (long long)a->d);
     return KS_ERR_INVALID_CONFIG;
   }
@@ -928,7 +951,9 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
   const uint64_t bh = uint64_t(a->batch * a->heads);
   const float scale = a->scale > 0.f ? a->scale : 1.f / sqrtf(float(a->d));
   const float scale_log2 = scale * 1.4426950408889634f;
-  if (a->d != kD || !aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) {
+  // tensor cores: d = 128 with either config, d = 64 with two query tiles per CTA
+  const bool tc_d = a->d == kD || (a->d == 64 && cfg->tile_m == 256);
+  if (!tc_d || !aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) {
     dim3 grid(unsigned((a->nq + 3) / 4), unsigned(bh));
     fa_simt_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t *>(a->q), static_cast<const uint16_t *>(a->k),
@@ -937,14 +962,14 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
     return ks::map_cuda(cudaGetLastError());
   }
   CUtensorMap tq, tk, tv;
-  const uint64_t rs = kD * 2;
-  s = ks::encode_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->q, kD, uint64_t(a->nq), bh, rs,
+  const uint64_t d = uint64_t(a->d), rs = d * 2;
+  s = ks::encode_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->q, d, uint64_t(a->nq), bh, rs,
                          rs * uint64_t(a->nq), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s == KS_OK)
-    s = ks::encode_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->k, kD, uint64_t(a->nk), bh, rs,
+    s = ks::encode_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->k, d, uint64_t(a->nk), bh, rs,
                            rs * uint64_t(a->nk), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s == KS_OK)
-    s = ks::encode_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->v, kD, uint64_t(a->nk), bh, rs,
+    s = ks::encode_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->v, d, uint64_t(a->nk), bh, rs,
                            rs * uint64_t(a->nk), 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != KS_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -958,17 +983,12 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
         ks::wait_ctx());
     return ks::map_cuda(cudaGetLastError());
   }
-  cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(FaLayout::smem_request));
-  if (e != cudaSuccess) return ks::map_cuda(e);
   // persistent: one CTA per SM (fewer when there are fewer work items)
   const int64_t items = ((a->nq + 2 * kTile - 1) / (2 * kTile)) * int64_t(bh);
   const int sms = ks::sm_count();
   const unsigned grid = unsigned(items < sms ? items : sms);
-  fa_fwd_kernel<<<grid, kThreads2, FaLayout::smem_request, st>>>(
-      tq, tk, tv, static_cast<uint16_t *>(a->out), int(a->nq), int(a->nk), int(bh), scale_log2, cfg->causal,
-      ks::wait_ctx());
-  return ks::map_cuda(cudaGetLastError());
+  return a->d == kD ? launch_fwd<kD>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal)
+                    : launch_fwd<64>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal);
 }
 
 }  // extern "C"

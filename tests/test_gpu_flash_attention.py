@@ -51,7 +51,7 @@ def _check_mh(o, q, k, v, causal):
     b, h = q.shape[:2]
     rho = np.stack([orf.attention_abs_weight(q[i, j], k[i, j], v[i, j], causal=causal)
                     for i in range(b) for j in range(h)]).reshape(exp.shape)
-    if q.shape[-1] == 128:
+    if q.shape[-1] in (64, 128):  # tensor-core path: P enters the MMA as bf16
         assert_attention_close(o, exp, rho)
     else:
         assert_bf16_close(o, exp)
@@ -74,6 +74,28 @@ def test_attention_multihead(ks, shape, causal, tile_m):
     cfg = N.FlashAttentionConfig(tile_m, 128, 2, int(causal))
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
     _check_mh(o, q, k, v, causal)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("shape", [(1, 1, 256, 256, 64), (2, 3, 384, 384, 64), (1, 2, 300, 300, 64),
+                                   (1, 1, 1, 1, 64), (1, 1, 129, 129, 64), (1, 2, 200, 520, 64),
+                                   (1, 1, 520, 200, 64)])
+def test_attention_d64_tensor_cores(ks, shape, causal):
+    """d = 64 on the tcgen05 kernel (two query tiles per CTA): one 64-column
+    box per tile, P V with N = 64."""
+    N, ops = ks
+    q, k, v = _mh(shape, 11)
+    cfg = N.FlashAttentionConfig(256, 128, 2, int(causal))
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
+    _check_mh(o, q, k, v, causal)
+
+
+def test_attention_d64_large_logits(ks):
+    N, ops = ks
+    q, k, v = _mh((1, 2, 512, 512, 64), 12, scale=4.0)
+    cfg = N.FlashAttentionConfig(256, 128, 2, 1)
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=True, cfg=cfg))
+    _check_mh(o, q, k, v, True)
 
 
 @pytest.mark.parametrize("tile_m", [256, 128])
