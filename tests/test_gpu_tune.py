@@ -67,6 +67,7 @@ def test_softmax_pipeline_gate_injection_and_cache(tune, tmp_path):
     ("reduction", [1 << 24], {}),
     ("reduction", [4099, 512], {}),
     ("flash_attention", [1, 4, 512, 128], {"causal": True}),
+    ("flash_attention", [1, 4, 512, 64], {"causal": True}),
     ("flash_attention", [96, 160, 32], {}),
 ])
 def test_family_pipelines(tune, tmp_path, family, shape, extra):
