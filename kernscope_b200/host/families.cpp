@@ -399,7 +399,7 @@ class FlashSession : public Session {
   // per element |a - r| <= 1e-2 * rho, rho = softmax |V| (row weights of |V|).
   GateVerdict verdict(const std::vector<float> &got, const std::vector<float> &ref) const override {
     GateVerdict gv = bf16_verdict(got, ref);
-    if (sh.d != 128) return gv;
+    if (sh.d != 128 && sh.d != 64) return gv;  // only d = 64 and 128 can take the tensor-core path
     double worst = 0.0;
     const float scale = 1.f / std::sqrt(float(sh.d));
     std::vector<float> srow(static_cast<size_t>(sh.nk));
@@ -439,6 +439,12 @@ class FlashSession : public Session {
   int corrupt_output(void *st) override { return ks_gpu_memset(dout.p, 0, dout.bytes, st); }
 };
 
+// The tcgen05 kernels take d = 128 with either tile_m and d = 64 with tile_m
+// 256; every other (config, d) runs on the CUDA-core kernel.
+static bool fa_tensor_path(const FlashAttentionConfig &c, std::int64_t d) {
+  return d == 128 || (d == 64 && c.tile_m == 256);
+}
+
 class FlashFamily : public Family {
  public:
   bool causal = false;
@@ -472,11 +478,13 @@ class FlashFamily : public Family {
   }
   Resources resources(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
-    if (f.d != 128) return Resources{48, 4 * 256 * 4, 128, 0};
     const FlashAttentionConfig c = typed(cfg, causal);
+    if (!fa_tensor_path(c, f.d)) return Resources{48, 4 * 256 * 4, 128, 0};
     // tile_m 256: three warpgroups (the producer/MMA one hands registers to
     // the two softmax ones); tile_m 128: ten warps
-    return Resources{168, int(smem_bytes(c, FlashAttentionProblem{})), c.tile_m == 256 ? 384 : 320, 512};
+    FlashAttentionProblem p{};
+    p.d = f.d;
+    return Resources{168, int(smem_bytes(c, p)), c.tile_m == 256 ? 384 : 320, 512};
   }
   LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
     const FaShape f = fa_shape(s);
@@ -947,12 +955,13 @@ std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
          16 + 1024;
 }
 
-std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProblem &) noexcept {
-  // tile_m 256: Q0, Q1 and a 2-stage K/V ring of 128 x 128 bf16 tiles;
+std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProblem &p) noexcept {
+  // tile_m 256: Q0, Q1 and a 2-stage K/V ring of 128 x d bf16 tiles;
   // tile_m 128: one Q tile, the K/V ring and the row-statistics exchange
   // (3 KB); plus barriers and alignment slack
   if (c.tile_m == 128) return 5 * 32768 + 3072 + 16 * 8 + 16 + 1024;
-  return 6 * 32768 + 16 * 8 + 16 + 1024;
+  const std::int64_t tile = p.d == 64 ? 16384 : 32768;
+  return 6 * tile + 16 * 8 + 16 + 1024;
 }
 
 LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) noexcept {
@@ -974,10 +983,14 @@ LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttenti
     g.grid_x = int(std::min<std::int64_t>(std::int64_t(g.grid_x) * g.grid_y, 148));
     g.grid_y = 1;
   }
-  g.block_x = p.d != 128 ? 128 : c.tile_m == 256 ? 384 : 320;
-  if (p.d != 128) g.grid_x = int((p.nq + 3) / 4);
-  g.smem_bytes = p.d == 128 ? int(smem_bytes(c, p)) : 4 * 256 * 4;
-  g.tmem_columns = p.d == 128 ? 512 : 0;
+  const bool tc = fa_tensor_path(c, p.d);
+  g.block_x = !tc ? 128 : c.tile_m == 256 ? 384 : 320;
+  if (!tc) {
+    g.grid_x = int((p.nq + 3) / 4);
+    g.grid_y = int(p.batch_heads);
+  }
+  g.smem_bytes = tc ? int(smem_bytes(c, p)) : 4 * 256 * 4;
+  g.tmem_columns = tc ? 512 : 0;
   return g;
 }
 
