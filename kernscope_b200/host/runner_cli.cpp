@@ -12,7 +12,10 @@
 // kernel_symbol() names it, e.g. kernscope_b200_softmax_b256_v8_onepass)
 // selects the config; without --kernel the family's default config runs.
 // --grid / --block are accepted for compatibility and ignored (the launch
-// geometry follows from the config).  Inputs and output are raw row-major
+// geometry follows from the config).  So that the reference's gate script
+// can drive this runner unchanged, --hsaco is accepted and ignored too, and
+// without --family the family is read from the symbol's prefix
+// (kernscope_b200_<family>_...).  Inputs and output are raw row-major
 // bf16 buffers and the --int scalars come in the reference's order:
 //
 //   softmax    (x)            -> out   ints rows, cols
@@ -51,10 +54,23 @@ struct Options {
 int usage(const char *msg) {
   if (msg) std::fprintf(stderr, "ks-template-runner: %s\n", msg);
   std::fprintf(stderr,
-               "usage: ks-template-runner --family <softmax|layernorm|bias_gelu|reduction|matmul|attention>\n"
+               "usage: ks-template-runner [--family <softmax|layernorm|bias_gelu|reduction|matmul|attention>]\n"
                "       [--kernel <symbol>] [--causal] [--gelu erf|tanh] [--grid <W[xH]>] [--block <X[xY]>]\n"
                "       [--in <bin>]... --out <bin> --out-size <bytes> [--int <i32>]...\n");
   return 2;
+}
+
+// The runner's family name for a symbol kernscope_b200_<family>_..., or "".
+std::string family_of_symbol(const std::string &sym) {
+  const std::string pre = "kernscope_b200_";
+  if (sym.compare(0, pre.size(), pre) != 0) return "";
+  const std::string rest = sym.substr(pre.size());
+  static const std::pair<const char *, const char *> names[] = {
+      {"flash_attention_", "attention"}, {"bias_gelu_", "bias_gelu"}, {"layernorm_", "layernorm"},
+      {"softmax_", "softmax"},           {"reduction_", "reduction"}, {"matmul_", "matmul"}};
+  for (const auto &[prefix, fam] : names)
+    if (rest.compare(0, std::string(prefix).size(), prefix) == 0) return fam;
+  return "";
 }
 
 int fail(const std::string &what, int status) {
@@ -134,12 +150,14 @@ static int run_main(int argc, char **argv) {
       if (s == "--in") o.inputs.push_back(v);
       if (s == "--out-size") o.out_size = std::size_t(std::strtoull(v, nullptr, 10));
       if (s == "--int") o.ints.push_back(std::strtoll(v, nullptr, 10));
-      if (s == "--hsaco") return usage("--hsaco is the HIP runner's flag; pass --family (configs are prebuilt)");
+      // --hsaco: the HIP module path of the reference runner; nothing to load here
     } else {
       return usage(("unknown argument " + s).c_str());
     }
   }
-  if (o.family.empty() || o.out.empty() || o.out_size == 0) return usage("--family, --out and --out-size are required");
+  if (o.family.empty()) o.family = family_of_symbol(o.kernel);
+  if (o.family.empty() || o.out.empty() || o.out_size == 0)
+    return usage("--family (or a kernscope_b200_<family>_ --kernel symbol), --out and --out-size are required");
   if (o.gelu != "erf" && o.gelu != "tanh") return usage("--gelu must be erf or tanh");
   // the symbol names the variant of the families that have one
   if (o.kernel.find("_causal") != std::string::npos) o.causal = true;

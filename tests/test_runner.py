@@ -36,8 +36,9 @@ def _run(*args):
 def test_usage_errors():
     assert _run().returncode == 2
     assert _run("--family", "softmax", "--out", "/tmp/x", "--out-size", "16", "--int", "2").returncode == 2
-    r = _run("--hsaco", "k.hsaco", "--family", "softmax", "--out", "/tmp/x", "--out-size", "16")
-    assert r.returncode == 2 and "prebuilt" in r.stderr
+    # no --family and a symbol that names none
+    r = _run("--hsaco", "k.hsaco", "--kernel", "kernscope_tune_softmax", "--out", "/tmp/x", "--out-size", "16")
+    assert r.returncode == 2 and "--family" in r.stderr
     r = _run("--family", "softmax", "--kernel", "not_a_symbol", "--out", "/tmp/x", "--out-size", "64",
              "--int", "4", "--int", "8")
     assert r.returncode == 2 and "unknown kernel symbol" in r.stderr
@@ -51,6 +52,24 @@ def test_no_device_fails_loudly(tmp_path):
     x = tmp_path / "x.bin"
     x.write_bytes(b"\0" * 64)
     r = _run("--family", "softmax", "--in", x, "--out", tmp_path / "o.bin", "--out-size", "64", "--int", "4",
+             "--int", "8")
+    assert r.returncode == 1 and "no CUDA device" in r.stderr
+
+
+def test_reference_gate_argv_reaches_the_device(tmp_path):
+    """The argument list the reference's gate script builds
+    (kernels/templates/tests/run_hip_gate.py: --hsaco, --kernel, --grid,
+    --block, --in..., --out, --out-size, --int...) is accepted as it is: the
+    family comes from the symbol and --hsaco is ignored.  Without a GPU the
+    run gets as far as the device check."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present (the GPU test runs the kernel)")
+    x = tmp_path / "x.bin"
+    x.write_bytes(b"\0" * 64)
+    r = _run("--hsaco", tmp_path / "unused.hsaco", "--kernel", "kernscope_b200_softmax_b256_v8_onepass", "--grid",
+             "4", "--block", "256", "--in", x, "--out", tmp_path / "o.bin", "--out-size", "64", "--int", "4",
              "--int", "8")
     assert r.returncode == 1 and "no CUDA device" in r.stderr
 
@@ -103,3 +122,26 @@ def test_runner_selects_config_by_symbol(cuda_ok, tmp_path, symbol):
     assert r.returncode == 0 and symbol in r.stdout, r.stdout + r.stderr
     got = np.frombuffer(out.read_bytes(), dtype=fx["expected"].dtype).reshape(fx["expected"].shape)
     assert_bf16_close(got, fx["expected"], gate=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fixture,symbol", [("softmax_32x512_s0", "kernscope_b200_softmax_b256_v8_onepass"),
+                                            ("matmul_64x64x64_s0", "kernscope_b200_matmul_m128_n256_k64_s4_a2_g16")])
+def test_reference_gate_argv(cuda_ok, tmp_path, fixture, symbol):
+    """The reference gate script's argument list, unchanged: --hsaco (any
+    path), --kernel with one of this library's symbols, no --family."""
+    path = [p for p in fixture_paths() if os.path.basename(p).startswith(fixture)][0]
+    fx = load_fixture(path)
+    names, ints = ARGS[fx["family"]]
+    ins = []
+    for n in names:
+        p = tmp_path / f"{n}.bin"
+        p.write_bytes(np.ascontiguousarray(fx[n]).tobytes())
+        ins += ["--in", p]
+    out = tmp_path / "out.bin"
+    exp = fx["expected"]
+    r = _run("--hsaco", tmp_path / "module.hsaco", "--kernel", symbol, "--grid", "1", "--block", "1", *ins,
+             "--out", out, "--out-size", exp.nbytes, *sum((["--int", v] for v in ints(fx["shape"])), []))
+    assert r.returncode == 0 and symbol in r.stdout, r.stdout + r.stderr
+    got = np.frombuffer(out.read_bytes(), dtype=exp.dtype).reshape(exp.shape)
+    assert_bf16_close(got, exp, gate=True)
