@@ -13,6 +13,7 @@
 //   partials in the workspace, last CTA sums them in order and writes the
 //   fp32 result (and the fp64 value for a cross-GPU combine).
 // Both are HBM-bound: 4 (fp32) or 2 (bf16) bytes read per element.
+#include <algorithm>
 #include <mutex>
 
 #include "ks_common.cuh"
@@ -151,12 +152,15 @@ __global__ void __launch_bounds__(1024) sum_axis0_kernel(const void *__restrict_
   if (active) {
     const int64_t rstep = int64_t(TY) * gridDim.y;
     int64_t r = int64_t(blockIdx.y) * TY + ty;
-    for (; r + rstep < rows; r += 2 * rstep) {
-      float a[VEC], b[VEC];
+    // four rows per iteration keep four 16-byte loads per thread in flight
+    for (; r + 3 * rstep < rows; r += 4 * rstep) {
+      float a[VEC], b[VEC], c2[VEC], d[VEC];
       load_cols<VEC, BF16_IN>(x, r * cols + cvec * VEC, a);
       load_cols<VEC, BF16_IN>(x, (r + rstep) * cols + cvec * VEC, b);
+      load_cols<VEC, BF16_IN>(x, (r + 2 * rstep) * cols + cvec * VEC, c2);
+      load_cols<VEC, BF16_IN>(x, (r + 3 * rstep) * cols + cvec * VEC, d);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) acc[j] += a[j] + b[j];
+      for (int j = 0; j < VEC; ++j) acc[j] += (a[j] + b[j]) + (c2[j] + d[j]);
     }
     for (; r < rows; r += rstep) {
       float a[VEC];
@@ -276,16 +280,24 @@ int plan(const ks_reduction_config &c, const ks_reduction_args &a, Plan &p, char
                      c.vec_width);
       return KS_ERR_INVALID_CONFIG;
     }
+    // A strip is at most 32 vectors wide (256 columns at vec_width 8): one
+    // warp spans it, or several rows of it when the rows are narrower; the
+    // block's other threads take further rows of the same strip.  Rows are
+    // split over gridDim.y CTAs until about 8 CTAs per SM are in flight,
+    // but no further than keeps each strip's combine (split x strip width
+    // fp32 partials, read by the strip's last CTA) within 128 KB.
     const int64_t nvec = a.cols / c.vec_width;
-    int tx = 32;
-    while (tx < c.block && tx < nvec) tx <<= 1;
-    if (tx > c.block) tx = c.block;
+    int tx = 1;
+    while (tx < 32 && tx < nvec) tx <<= 1;
     p.tx = tx;
     p.ty = c.block / tx;
     p.n_strips = (nvec + tx - 1) / tx;
-    const int64_t want = (4LL * sms + p.n_strips - 1) / p.n_strips;
+    const int64_t width = std::min<int64_t>(int64_t(tx) * c.vec_width, a.cols);
+    const int64_t want = (8LL * sms + p.n_strips - 1) / p.n_strips;
     const int64_t max_split = (a.rows + int64_t(p.ty) * 8 - 1) / (int64_t(p.ty) * 8);
+    const int64_t combine_cap = (128 * 1024 / 4) / width;
     int64_t split = want < max_split ? want : max_split;
+    if (split > combine_cap) split = combine_cap;
     if (split > 65535) split = 65535;
     if (split < 1) split = 1;
     p.split = int(split);
