@@ -767,7 +767,11 @@ class RowFamily : public Family {
     const auto [r, c] = rc(s);
     (void)r;
     Resources res{64, 512, block, 0};
-    if (kind == RowKind::kReduction) res.regs_per_thread = 40;
+    if (kind == RowKind::kReduction) {
+      res.regs_per_thread = 40;
+      // axis 0 stages every thread's column partials (block x vec_width fp32)
+      if (axis_of(s) == 0) res.smem_bytes = block * iget(cfg, "vec_width", 8) * 4 + 16;
+    }
     if (kind == RowKind::kBiasGelu) res.regs_per_thread = 61;
     if (mode == KS_MODE_STAGED) {
       const std::int64_t stride = (c * 2 + 127) / 128 * 128;
