@@ -337,6 +337,129 @@ __global__ void __launch_bounds__(MAXB) layernorm_onepass_v8_kernel(const uint16
 }
 
 // ===========================================================================
+// Short rows (at most 1024 columns, 8-wide vectors): one warp per row, so
+// the reductions are warp shuffles with no block barrier, and a CTA of
+// blockDim.x / 32 warps keeps that many rows in flight plus each warp's
+// prefetched next row.  Lane l holds column chunks l, l+32, ... (WCH of
+// them).  Layernorm's gamma and beta chunks are the same for every row a
+// lane touches, so they stay in registers.
+// ===========================================================================
+template <int WCH>
+KS_DEV void load_row_warp8(const uint16_t *__restrict__ x, int r, int cols, int nvec, uint4 (&w)[WCH]) {
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + size_t(r) * cols);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < WCH; ++k)
+    if (lane + 32 * k < nvec) w[k] = __ldcs(xr + lane + 32 * k);
+}
+
+template <int WCH>
+__global__ void __launch_bounds__(256) softmax_warp_v8_kernel(const uint16_t *__restrict__ x,
+                                                              uint16_t *__restrict__ y, int rows, int cols) {
+  const int lane = threadIdx.x & 31, nvec = cols >> 3;
+  const int wpc = blockDim.x >> 5;
+  const int first = int(blockIdx.x) * wpc + (threadIdx.x >> 5), stride = int(gridDim.x) * wpc;
+  uint4 nxt[WCH];
+  if (first < rows) load_row_warp8<WCH>(x, first, cols, nvec, nxt);
+  for (int r = first; r < rows; r += stride) {
+    uint4 w[WCH];
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) w[k] = nxt[k];
+    if (r + stride < rows) load_row_warp8<WCH>(x, r + stride, cols, nvec, nxt);
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < WCH; ++k)
+      if (lane + 32 * k < nvec) m = fmaxf(m, max8_packed(w[k]));
+    m = ks_warp_max(m);
+    const float mL = m * kLog2e;
+    float e[WCH][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) {
+      if (lane + 32 * k < nvec) {
+        unpack8(w[k], e[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          e[k][j] = ks_ex2(fmaf(e[k][j], kLog2e, -mL));
+          sum += e[k][j];
+        }
+      }
+    }
+    const float inv = 1.f / ks_warp_sum(sum);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + size_t(r) * cols);
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) {
+      if (lane + 32 * k < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[k][j] *= inv;
+        __stcs(yr + lane + 32 * k, pack8(e[k]));
+      }
+    }
+  }
+}
+
+template <int WCH>
+__global__ void __launch_bounds__(256) layernorm_warp_v8_kernel(const uint16_t *__restrict__ x,
+                                                                const uint16_t *__restrict__ gamma,
+                                                                const uint16_t *__restrict__ beta,
+                                                                uint16_t *__restrict__ y, int rows, int cols,
+                                                                float inv_cols, float eps) {
+  const int lane = threadIdx.x & 31, nvec = cols >> 3;
+  const int wpc = blockDim.x >> 5;
+  const int first = int(blockIdx.x) * wpc + (threadIdx.x >> 5), stride = int(gridDim.x) * wpc;
+  uint4 gw[WCH], bw[WCH];
+#pragma unroll
+  for (int k = 0; k < WCH; ++k)
+    if (lane + 32 * k < nvec) {
+      gw[k] = __ldg(reinterpret_cast<const uint4 *>(gamma) + lane + 32 * k);
+      bw[k] = __ldg(reinterpret_cast<const uint4 *>(beta) + lane + 32 * k);
+    }
+  uint4 nxt[WCH];
+  if (first < rows) load_row_warp8<WCH>(x, first, cols, nvec, nxt);
+  for (int r = first; r < rows; r += stride) {
+    uint4 w[WCH];
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) w[k] = nxt[k];
+    if (r + stride < rows) load_row_warp8<WCH>(x, r + stride, cols, nvec, nxt);
+    float v[WCH][8];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) {
+      if (lane + 32 * k < nvec) {
+        unpack8(w[k], v[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[k][j];
+      }
+    }
+    const float mean = ks_warp_sum(s) * inv_cols;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) {
+      if (lane + 32 * k < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[k][j] -= mean;
+          q = fmaf(v[k][j], v[k][j], q);
+        }
+      }
+    }
+    const float rstd = rsqrtf(ks_warp_sum(q) * inv_cols + eps);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + size_t(r) * cols);
+#pragma unroll
+    for (int k = 0; k < WCH; ++k) {
+      if (lane + 32 * k < nvec) {
+        float g[8], b[8];
+        unpack8(gw[k], g);
+        unpack8(bw[k], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[k][j] = fmaf(v[k][j], rstd * g[j], b[j]);
+        __stcs(yr + lane + 32 * k, pack8(v[k]));
+      }
+    }
+  }
+}
+
+// ===========================================================================
 // softmax
 // ===========================================================================
 // ONEPASS: thread t owns vector chunks t, t+B, ..., t+(MAXCH-1)B of the row
@@ -807,6 +930,24 @@ int grid_for(K kernel, int block, int64_t work, size_t dyn_smem = 0) {
   return int(work < cap ? work : cap);
 }
 
+// ONEPASS rows of at most this many columns (8-wide vectors) run one row per
+// warp (softmax_warp_v8_kernel, layernorm_warp_v8_kernel).  Longer rows
+// would hold more than 4 chunks per lane and cost the occupancy that keeps
+// rows in flight.
+constexpr int64_t kWarpRowCols = 1024;
+// 16-byte chunks per lane for a warp-held row: 1, 2 or 4.
+int warp_chunks(int64_t cols) {
+  const int64_t per_lane = (cols / 8 + 31) / 32;
+  return per_lane <= 1 ? 1 : per_lane <= 2 ? 2 : 4;
+}
+// A resident grid of `block`-thread CTAs over rows (one row per warp).
+template <typename... KArgs, typename... Args>
+int launch_rows_warp(void (*k)(KArgs...), int block, int64_t rows, cudaStream_t st, Args... args) {
+  const int64_t ctas = (rows + block / 32 - 1) / (block / 32);
+  k<<<grid_for(k, block, ctas), block, 0, st>>>(static_cast<KArgs>(args)...);
+  return ks::map_cuda(cudaGetLastError());
+}
+
 int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, int64_t cols, char *reason,
                    size_t len) {
   if (!valid_block(block)) {
@@ -865,6 +1006,14 @@ int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, c
   } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = softmax_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, y, a.rows, a.cols);
+  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < (int64_t(1) << 31)) {
+    const int block = cfg.block < 256 ? cfg.block : 256;
+    switch (warp_chunks(a.cols)) {
+      case 1: return launch_rows_warp(softmax_warp_v8_kernel<1>, block, a.rows, st, x, y, int(a.rows), int(a.cols));
+      case 2: return launch_rows_warp(softmax_warp_v8_kernel<2>, block, a.rows, st, x, y, int(a.rows), int(a.cols));
+      default:
+        return launch_rows_warp(softmax_warp_v8_kernel<4>, block, a.rows, st, x, y, int(a.rows), int(a.cols));
+    }
   } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
     auto k = cfg.block <= 256 ? softmax_onepass_v8_kernel<kRegElems / 8, 256>
                               : softmax_onepass_v8_kernel<kRegElems / 8, 1024>;
@@ -900,6 +1049,20 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
   } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = layernorm_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, g, b, y, a.rows, a.cols, eps);
+  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < (int64_t(1) << 31)) {
+    const int block = cfg.block < 256 ? cfg.block : 256;
+    const float ic = 1.f / float(a.cols);
+    switch (warp_chunks(a.cols)) {
+      case 1:
+        return launch_rows_warp(layernorm_warp_v8_kernel<1>, block, a.rows, st, x, g, b, y, int(a.rows), int(a.cols),
+                                ic, eps);
+      case 2:
+        return launch_rows_warp(layernorm_warp_v8_kernel<2>, block, a.rows, st, x, g, b, y, int(a.rows), int(a.cols),
+                                ic, eps);
+      default:
+        return launch_rows_warp(layernorm_warp_v8_kernel<4>, block, a.rows, st, x, g, b, y, int(a.rows), int(a.cols),
+                                ic, eps);
+    }
   } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
     auto k = cfg.block <= 256 ? layernorm_onepass_v8_kernel<kRegElems / 8, 256>
                               : layernorm_onepass_v8_kernel<kRegElems / 8, 1024>;

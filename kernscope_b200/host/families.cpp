@@ -778,6 +778,12 @@ class RowFamily : public Family {
       const int stages = int(std::min<std::int64_t>(8, 65536 / std::max<std::int64_t>(stride, 1)));
       res.smem_bytes = int(stride * (stages + (kind == RowKind::kLayerNorm ? 2 : 0))) + 512;
       res.regs_per_thread = 80;
+    } else if (iget(cfg, "vec_width", 8) == 8 && mode == KS_MODE_ONEPASS && c <= 1024 &&
+               (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm)) {
+      // one row per warp, at most 256 threads per CTA; layernorm also keeps
+      // its gamma/beta chunks in registers
+      res.block = std::min(block, 256);
+      res.regs_per_thread = kind == RowKind::kSoftmax ? 80 : c <= 512 ? 76 : 145;
     } else if (block <= 256 && iget(cfg, "vec_width", 8) == 8 && kind != RowKind::kReduction &&
                kind != RowKind::kBiasGelu) {
       res.regs_per_thread = 80;  // the prefetching 8-wide instantiation

@@ -70,6 +70,17 @@ def test_softmax_ragged(ks, shape):
     assert_bf16_close(y, orf.softmax(inp["x"]))
 
 
+@pytest.mark.parametrize("shape", [(4099, 256), (1000, 520), (777, 1024), (70000, 64), (129, 8)])
+@pytest.mark.parametrize("block", [128, 256, 1024])
+def test_softmax_warp_rows(ks, shape, block):
+    """Rows of at most 1024 columns run one row per warp: 1, 2 or 4 chunks
+    per lane, partly filled warps, and more rows than resident warps."""
+    N, ops = ks
+    inp = oin.generate_inputs("softmax", shape, seed=9)
+    y = to_numpy(ops.softmax(to_torch(inp["x"]), cfg=N.SoftmaxConfig(block, 8, N.KS_MODE_ONEPASS)))
+    assert_bf16_close(y, orf.softmax(inp["x"]))
+
+
 def test_softmax_rejects_bad_config(ks):
     N, ops = ks
     st, reason = N.validate("softmax", N.SoftmaxConfig(96, 8, 0), 4, 64)
@@ -113,6 +124,16 @@ def test_layernorm_ragged(ks, shape):
     _, ops = ks
     inp = oin.generate_inputs("layernorm", shape, seed=6)
     y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta"))))
+    assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
+
+
+@pytest.mark.parametrize("shape", [(4099, 256), (1000, 520), (777, 1024), (70000, 64), (129, 8)])
+@pytest.mark.parametrize("block", [128, 256, 1024])
+def test_layernorm_warp_rows(ks, shape, block):
+    N, ops = ks
+    inp = oin.generate_inputs("layernorm", shape, seed=10)
+    cfg = N.LayerNormConfig(block, 8, N.KS_MODE_ONEPASS)
+    y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta")), cfg=cfg))
     assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
 
 
