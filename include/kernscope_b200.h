@@ -111,7 +111,10 @@ typedef enum ks_elem_mode {
   KS_MODE_TWOPASS = 1,
   KS_MODE_STRIDED = 2,  /* reduction: warp-shuffle combine */
   KS_MODE_TREE = 3,     /* reduction: shared-memory tree combine */
-  KS_MODE_STAGED = 4
+  KS_MODE_STAGED = 4,
+  KS_MODE_CLUSTER = 5   /* softmax, layernorm: one row over a cluster of 2-8
+                           CTAs, statistics combined through distributed
+                           shared memory (vec_width 8; long rows, few rows) */
 } ks_elem_mode;
 
 /* ---- softmax (tools/tune/include/kernscope/tune/softmax_gen.h:39-51) ----

@@ -212,6 +212,17 @@ KS_DEV uint32_t ks_cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+KS_DEV uint32_t ks_cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// fp32 load from another CTA's shared memory (address from ks_mapa).
+KS_DEV float ks_ld_shared_cluster_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 KS_DEV uint32_t ks_mapa(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;

@@ -460,6 +460,134 @@ __global__ void __launch_bounds__(256) layernorm_warp_v8_kernel(const uint16_t *
 }
 
 // ===========================================================================
+// Long rows over a thread-block cluster (mode CLUSTER).  CTA rank r of a
+// cluster of cs CTAs holds columns [r*seg, (r+1)*seg) of one row in
+// registers (CH 8-wide chunks per thread).  The row statistics -- max and
+// sum for softmax, sum and sum of squared deviations for layernorm --
+// combine across the cluster through distributed shared memory between
+// cluster barriers.  The row is read from HBM once however long it is, and
+// a few rows still fill the 148 SMs.
+// ===========================================================================
+// This CTA's partial v (the same in every thread) combined over the cluster:
+// publish it in `slot`, wait for every CTA, and let warp 0 gather the cs
+// partials.  Each combine of a kernel uses its own slot.
+KS_DEV float cluster_combine(float v, float *slot, float *bcast, bool is_max) {
+  if (threadIdx.x == 0) *slot = v;
+  ks_cluster_sync();
+  if (threadIdx.x < 32) {
+    const uint32_t cs = ks_cluster_nctarank();
+    float t = is_max ? -INFINITY : 0.f;
+    if (threadIdx.x < cs) t = ks_ld_shared_cluster_f32(ks_mapa(ks_smem_u32(slot), threadIdx.x));
+    t = is_max ? ks_warp_max(t) : ks_warp_sum(t);
+    if (threadIdx.x == 0) *bcast = t;
+  }
+  __syncthreads();
+  return *bcast;
+}
+
+template <int CH>
+__global__ void __launch_bounds__(1024) softmax_cluster_v8_kernel(const uint16_t *__restrict__ x,
+                                                                  uint16_t *__restrict__ y, int64_t cols, int seg) {
+  __shared__ float sh_max[32], sh_sum[32];
+  __shared__ float slot_a, slot_b, bcast;
+  const uint32_t cs = ks_cluster_nctarank(), rank = ks_cluster_ctarank();
+  const int64_t off = int64_t(blockIdx.x / cs) * cols + int64_t(rank) * seg;
+  const int t = threadIdx.x, nt = blockDim.x, nvec = seg >> 3;
+  const uint4 *xs = reinterpret_cast<const uint4 *>(x + off);
+  uint4 w[CH];
+#pragma unroll
+  for (int k = 0; k < CH; ++k)
+    if (t + k * nt < nvec) w[k] = __ldcs(xs + t + k * nt);
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < CH; ++k)
+    if (t + k * nt < nvec) m = fmaxf(m, max8_packed(w[k]));
+  m = cluster_combine(block_max_fast(m, sh_max), &slot_a, &bcast, true);
+  const float mL = m * kLog2e;
+  float e[CH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    if (t + k * nt < nvec) {
+      unpack8(w[k], e[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        e[k][j] = ks_ex2(fmaf(e[k][j], kLog2e, -mL));
+        s += e[k][j];
+      }
+    }
+  }
+  const float inv = 1.f / cluster_combine(block_sum_fast(s, sh_sum), &slot_b, &bcast, false);
+  uint4 *ys = reinterpret_cast<uint4 *>(y + off);
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    if (t + k * nt < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[k][j] *= inv;
+      __stcs(ys + t + k * nt, pack8(e[k]));
+    }
+  }
+  ks_cluster_sync();  // no CTA leaves while another may still read its slots
+}
+
+template <int CH>
+__global__ void __launch_bounds__(1024) layernorm_cluster_v8_kernel(const uint16_t *__restrict__ x,
+                                                                    const uint16_t *__restrict__ gamma,
+                                                                    const uint16_t *__restrict__ beta,
+                                                                    uint16_t *__restrict__ y, int64_t cols, int seg,
+                                                                    float inv_cols, float eps) {
+  __shared__ float sh_a[32], sh_b[32];
+  __shared__ float slot_a, slot_b, bcast;
+  const uint32_t cs = ks_cluster_nctarank(), rank = ks_cluster_ctarank();
+  const int64_t off = int64_t(blockIdx.x / cs) * cols + int64_t(rank) * seg;
+  const int t = threadIdx.x, nt = blockDim.x, nvec = seg >> 3;
+  const uint4 *xs = reinterpret_cast<const uint4 *>(x + off);
+  uint4 w[CH];
+#pragma unroll
+  for (int k = 0; k < CH; ++k)
+    if (t + k * nt < nvec) w[k] = __ldcs(xs + t + k * nt);
+  float v[CH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    if (t + k * nt < nvec) {
+      unpack8(w[k], v[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[k][j];
+    }
+  }
+  const float mean = cluster_combine(block_sum_fast(s, sh_a), &slot_a, &bcast, false) * inv_cols;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    if (t + k * nt < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[k][j] -= mean;
+        q = fmaf(v[k][j], v[k][j], q);
+      }
+    }
+  }
+  const float rstd = rsqrtf(cluster_combine(block_sum_fast(q, sh_b), &slot_b, &bcast, false) * inv_cols + eps);
+  const uint4 *g4 = reinterpret_cast<const uint4 *>(gamma + int64_t(rank) * seg);
+  const uint4 *b4 = reinterpret_cast<const uint4 *>(beta + int64_t(rank) * seg);
+  uint4 *ys = reinterpret_cast<uint4 *>(y + off);
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = t + k * nt;
+    if (c < nvec) {
+      float g[8], b[8];
+      unpack8(__ldg(g4 + c), g);
+      unpack8(__ldg(b4 + c), b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] = fmaf(v[k][j], rstd * g[j], b[j]);
+      __stcs(ys + c, pack8(v[k]));
+    }
+  }
+  ks_cluster_sync();  // no CTA leaves while another may still read its slots
+}
+
+// ===========================================================================
 // softmax
 // ===========================================================================
 // ONEPASS: thread t owns vector chunks t, t+B, ..., t+(MAXCH-1)B of the row
@@ -948,6 +1076,38 @@ int launch_rows_warp(void (*k)(KArgs...), int block, int64_t rows, cudaStream_t 
   return ks::map_cuda(cudaGetLastError());
 }
 
+// Cluster size for mode CLUSTER, or 0 when the row cannot be spread: each
+// CTA's share of the row (seg = cols / cs) is a multiple of 8 columns and
+// holds at most 32 bf16 per thread (16 while the cluster can still grow);
+// clusters stay within the portable 8 CTAs and grow while rows x cs leaves
+// fewer than two CTAs per SM.
+int cluster_plan(int block, int64_t rows, int64_t cols) {
+  if (cols % 8 != 0 || block < 256) return 0;
+  int cs = 2;
+  while (cs < 8 && cols > int64_t(block) * 16 * cs) cs <<= 1;
+  while (cs < 8 && rows * cs < 2 * 148 && cols % (int64_t(cs) * 16) == 0 && cols / (cs * 2) >= int64_t(block) * 8)
+    cs <<= 1;
+  if (cols % (int64_t(cs) * 8) != 0 || cols > int64_t(block) * 32 * cs) return 0;
+  return cs;
+}
+
+// One cluster of cs CTAs per row.
+template <typename... KArgs, typename... Args>
+int launch_cluster(void (*k)(KArgs...), int cs, int64_t rows, int block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t c = {};
+  c.gridDim = dim3(unsigned(rows * cs));
+  c.blockDim = dim3(unsigned(block));
+  c.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = unsigned(cs);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  c.attrs = at;
+  c.numAttrs = 1;
+  return ks::map_cuda(cudaLaunchKernelEx(&c, k, static_cast<KArgs>(args)...));
+}
+
 int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, int64_t cols, char *reason,
                    size_t len) {
   if (!valid_block(block)) {
@@ -958,8 +1118,8 @@ int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, 
     ks::set_reason(reason, len, "%s: vec_width must be 1, 2, 4 or 8 (sm_100a space)", fam);
     return KS_ERR_INVALID_CONFIG;
   }
-  if (mode != KS_MODE_ONEPASS && mode != KS_MODE_TWOPASS && mode != KS_MODE_STAGED) {
-    ks::set_reason(reason, len, "%s: mode must be onepass, twopass or staged", fam);
+  if (mode != KS_MODE_ONEPASS && mode != KS_MODE_TWOPASS && mode != KS_MODE_STAGED && mode != KS_MODE_CLUSTER) {
+    ks::set_reason(reason, len, "%s: mode must be onepass, twopass, staged or cluster", fam);
     return KS_ERR_INVALID_CONFIG;
   }
   if (rows <= 0 || cols <= 0) {
@@ -977,6 +1137,13 @@ int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, 
                    mode == KS_MODE_STAGED ? "staged" : "onepass", (long long)cols, block, kRegElems);
     return KS_ERR_INVALID_CONFIG;
   }
+  if (mode == KS_MODE_CLUSTER && (vec != 8 || rows >= (int64_t(1) << 28) || cluster_plan(block, rows, cols) == 0)) {
+    ks::set_reason(reason, len,
+                   "%s: cluster spreads a row over at most 8 CTAs of 32 columns per thread: vec_width must be 8, "
+                   "block >= 256, and cols %lld must split into a multiple of 8 columns per CTA within %lld",
+                   fam, (long long)cols, (long long)(int64_t(block) * 32 * 8));
+    return KS_ERR_INVALID_CONFIG;
+  }
   if (mode == KS_MODE_STAGED && (vec != 8 || block > 512 || staged_stages(cols) < 2)) {
     ks::set_reason(reason, len,
                    "%s: staged copies whole rows with 16-byte bulk copies: vec_width must be 8, block <= 512 "
@@ -992,7 +1159,19 @@ template <int VEC>
 int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, cudaStream_t st) {
   auto x = static_cast<const uint16_t *>(a.x);
   auto y = static_cast<uint16_t *>(a.out);
-  if (cfg.mode == KS_MODE_STAGED) {
+  if (cfg.mode == KS_MODE_CLUSTER) {
+    if constexpr (VEC == 8) {
+      const int cs = cluster_plan(cfg.block, a.rows, a.cols);
+      const int seg = int(a.cols / cs);
+      if (seg / 8 <= cfg.block)
+        return launch_cluster(softmax_cluster_v8_kernel<1>, cs, a.rows, cfg.block, st, x, y, a.cols, seg);
+      if (seg / 8 <= 2 * cfg.block)
+        return launch_cluster(softmax_cluster_v8_kernel<2>, cs, a.rows, cfg.block, st, x, y, a.cols, seg);
+      return launch_cluster(softmax_cluster_v8_kernel<4>, cs, a.rows, cfg.block, st, x, y, a.cols, seg);
+    } else {
+      return KS_ERR_INVALID_CONFIG;
+    }
+  } else if (cfg.mode == KS_MODE_STAGED) {
     if constexpr (VEC == 8) {
       const int stages = staged_stages(a.cols);
       const size_t shm = size_t(stages) * size_t((a.cols * 2 + 127) & ~int64_t(127));
@@ -1033,7 +1212,23 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
   auto b = static_cast<const uint16_t *>(a.beta);
   auto y = static_cast<uint16_t *>(a.out);
   const float eps = a.eps > 0.f ? a.eps : 1e-5f;
-  if (cfg.mode == KS_MODE_STAGED) {
+  if (cfg.mode == KS_MODE_CLUSTER) {
+    if constexpr (VEC == 8) {
+      const int cs = cluster_plan(cfg.block, a.rows, a.cols);
+      const int seg = int(a.cols / cs);
+      const float ic = 1.f / float(a.cols);
+      if (seg / 8 <= cfg.block)
+        return launch_cluster(layernorm_cluster_v8_kernel<1>, cs, a.rows, cfg.block, st, x, g, b, y, a.cols, seg,
+                              ic, eps);
+      if (seg / 8 <= 2 * cfg.block)
+        return launch_cluster(layernorm_cluster_v8_kernel<2>, cs, a.rows, cfg.block, st, x, g, b, y, a.cols, seg,
+                              ic, eps);
+      return launch_cluster(layernorm_cluster_v8_kernel<4>, cs, a.rows, cfg.block, st, x, g, b, y, a.cols, seg, ic,
+                            eps);
+    } else {
+      return KS_ERR_INVALID_CONFIG;
+    }
+  } else if (cfg.mode == KS_MODE_STAGED) {
     if constexpr (VEC == 8) {
       const int stages = staged_stages(a.cols);
       const size_t shm = size_t(stages + 2) * size_t((a.cols * 2 + 127) & ~int64_t(127));

@@ -14,6 +14,7 @@ const char *mode_name(int m) {
     case KS_MODE_STRIDED: return "strided";
     case KS_MODE_TREE: return "tree";
     case KS_MODE_STAGED: return "staged";
+    case KS_MODE_CLUSTER: return "cluster";
     default: return "unknown";
   }
 }

@@ -113,7 +113,19 @@ int mode_from(const json &c, int dflt) {
   if (s == "strided") return KS_MODE_STRIDED;
   if (s == "tree") return KS_MODE_TREE;
   if (s == "staged") return KS_MODE_STAGED;
+  if (s == "cluster") return KS_MODE_CLUSTER;
   return dflt;
+}
+
+// CTAs a CLUSTER launch spreads one row over: the rule of the launch planner
+// in rowops.cu (2 to 8 CTAs, at most 16 columns per thread while the cluster
+// can grow, grown while rows x CTAs leave fewer than two per SM).
+std::int64_t cluster_ctas(int block, std::int64_t rows, std::int64_t cols) {
+  std::int64_t cs = 2;
+  while (cs < 8 && cols > std::int64_t(block) * 16 * cs) cs <<= 1;
+  while (cs < 8 && rows * cs < 2 * 148 && cols % (cs * 16) == 0 && cols / (cs * 2) >= std::int64_t(block) * 8)
+    cs <<= 1;
+  return cs;
 }
 
 }  // namespace
@@ -125,6 +137,7 @@ const char *elem_mode_name(ElemMode m) noexcept {
     case ElemMode::kStrided: return "strided";
     case ElemMode::kTree: return "tree";
     case ElemMode::kStaged: return "staged";
+    case ElemMode::kCluster: return "cluster";
   }
   return "unknown";
 }
@@ -735,7 +748,7 @@ class RowFamily : public Family {
     const std::vector<int> blocks = full ? std::vector<int>{128, 256, 512, 1024} : std::vector<int>{128, 256, 512};
     const std::vector<int> vecs = full ? std::vector<int>{1, 2, 4, 8} : std::vector<int>{4, 8};
     std::vector<std::string> modes;
-    if (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm) modes = {"onepass", "twopass", "staged"};
+    if (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm) modes = {"onepass", "twopass", "staged", "cluster"};
     if (kind == RowKind::kReduction) modes = {"strided", "tree"};
     for (int b : blocks)
       for (int vw : (axis_of(s) == -1 ? std::vector<int>{4} : vecs)) {
@@ -773,7 +786,10 @@ class RowFamily : public Family {
       if (axis_of(s) == 0) res.smem_bytes = block * iget(cfg, "vec_width", 8) * 4 + 16;
     }
     if (kind == RowKind::kBiasGelu) res.regs_per_thread = 61;
-    if (mode == KS_MODE_STAGED) {
+    if (mode == KS_MODE_CLUSTER) {
+      res.regs_per_thread = 50;  // up to four 8-wide chunks per thread
+      res.smem_bytes = 288;      // warp partials and the cluster slots
+    } else if (mode == KS_MODE_STAGED) {
       const std::int64_t stride = (c * 2 + 127) / 128 * 128;
       const int stages = int(std::min<std::int64_t>(8, 65536 / std::max<std::int64_t>(stride, 1)));
       res.smem_bytes = int(stride * (stages + (kind == RowKind::kLayerNorm ? 2 : 0))) + 512;
@@ -802,6 +818,8 @@ class RowFamily : public Family {
       const std::int64_t nvec = c / std::max(1, iget(cfg, "vec_width", 8));
       g.grid_x = int((nvec + g.block_x - 1) / g.block_x);
       g.grid_y = int((r + 31) / 32);
+    } else if (mode_from(cfg, -1) == KS_MODE_CLUSTER) {
+      g.grid_x = int(r * cluster_ctas(g.block_x, r, c));
     } else {
       g.grid_x = int(std::min<std::int64_t>(r, cap));
     }

@@ -57,7 +57,7 @@ struct FlashAttentionProblem {
   int dtype_bytes = 2;
 };
 enum class ElemMode : int { kOnePass = KS_MODE_ONEPASS, kTwoPass = KS_MODE_TWOPASS, kStrided = KS_MODE_STRIDED,
-                            kTree = KS_MODE_TREE, kStaged = KS_MODE_STAGED };
+                            kTree = KS_MODE_TREE, kStaged = KS_MODE_STAGED, kCluster = KS_MODE_CLUSTER };
 const char *elem_mode_name(ElemMode m) noexcept;
 struct ElemProblem {
   std::int64_t rows = 0, cols = 0;

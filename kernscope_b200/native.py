@@ -23,7 +23,7 @@ KS_ERR_DEVICE_TIMEOUT = -23
 KS_ERR_ARCH = -24
 
 KS_BF16, KS_F32, KS_F64 = 0, 1, 2
-KS_MODE_ONEPASS, KS_MODE_TWOPASS, KS_MODE_STRIDED, KS_MODE_TREE, KS_MODE_STAGED = 0, 1, 2, 3, 4
+KS_MODE_ONEPASS, KS_MODE_TWOPASS, KS_MODE_STRIDED, KS_MODE_TREE, KS_MODE_STAGED, KS_MODE_CLUSTER = 0, 1, 2, 3, 4, 5
 KS_GELU_ERF, KS_GELU_TANH = 0, 1
 
 MODE_NAMES = {"onepass": 0, "twopass": 1, "strided": 2, "tree": 3, "staged": 4}

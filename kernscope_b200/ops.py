@@ -35,14 +35,34 @@ def _pow2_block(cols: int, vec: int, per_thread: int) -> int:
     return b
 
 
-def default_softmax_config(cols: int) -> N.SoftmaxConfig:
+def _cluster_default(family: str, make, rows, cols: int):
+    """A few very long rows (at most 64 rows of 65536+ columns) leave most SMs
+    idle one CTA per row; spreading each row over a cluster measured
+    1590 -> 1987 GB/s (softmax) and 1310 -> 1778 GB/s (layernorm) at
+    64 x 131072 on B200.  With more rows the per-row CTAs win."""
+    if rows is None or rows > 64 or cols < 65536:
+        return None
+    for block in (512, 1024):
+        cfg = make(block, 8, N.KS_MODE_CLUSTER)
+        if N.validate(family, cfg, rows, cols)[0] == 0:
+            return cfg
+    return None
+
+
+def default_softmax_config(cols: int, rows: int | None = None) -> N.SoftmaxConfig:
+    c = _cluster_default("softmax", N.SoftmaxConfig, rows, cols)
+    if c is not None:
+        return c
     vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
     block = _pow2_block(cols, vec, 4)
     mode = N.KS_MODE_ONEPASS if cols <= block * 32 else N.KS_MODE_TWOPASS
     return N.SoftmaxConfig(block, vec, mode)
 
 
-def default_layernorm_config(cols: int) -> N.LayerNormConfig:
+def default_layernorm_config(cols: int, rows: int | None = None) -> N.LayerNormConfig:
+    c = _cluster_default("layernorm", N.LayerNormConfig, rows, cols)
+    if c is not None:
+        return c
     vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
     block = _pow2_block(cols, vec, 4)
     mode = N.KS_MODE_ONEPASS if cols <= block * 32 else N.KS_MODE_TWOPASS
@@ -75,7 +95,7 @@ def softmax(x: torch.Tensor, out=None, cfg=None, stream=None) -> torch.Tensor:
     _check_bf16_2d("x", x)
     rows, cols = x.shape
     out = torch.empty_like(x) if out is None else out
-    cfg = cfg or default_softmax_config(cols)
+    cfg = cfg or default_softmax_config(cols, rows)
     args = N.SoftmaxArgs(x.data_ptr(), out.data_ptr(), rows, cols)
     N.check("ks_softmax_launch", N.lib.ks_softmax_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
     return out
@@ -86,7 +106,7 @@ def layernorm(x, gamma, beta, eps: float = 1e-5, out=None, cfg=None, stream=None
         _check_bf16_2d(nm, t)
     rows, cols = x.shape
     out = torch.empty_like(x) if out is None else out
-    cfg = cfg or default_layernorm_config(cols)
+    cfg = cfg or default_layernorm_config(cols, rows)
     args = N.LayerNormArgs(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), rows, cols, eps)
     N.check("ks_layernorm_launch", N.lib.ks_layernorm_launch(C.byref(cfg), C.byref(args), _stream_ptr(stream)))
     return out

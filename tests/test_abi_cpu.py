@@ -53,6 +53,21 @@ def test_validate_rowops(N):
     assert N.validate("softmax", N.SoftmaxConfig(256, 8, 0), 0, 64)[0] == N.KS_ERR_INVALID_ARGS
 
 
+def test_validate_cluster_rows(N):
+    C = N.KS_MODE_CLUSTER
+    assert N.validate("softmax", N.SoftmaxConfig(1024, 8, C), 64, 131072) == (0, "")
+    assert N.validate("layernorm", N.LayerNormConfig(1024, 8, C), 2, 262144) == (0, "")
+    assert N.validate("layernorm", N.LayerNormConfig(256, 8, C), 1, 16) == (0, "")
+    for cfg, rows, cols in [
+        (N.SoftmaxConfig(1024, 4, C), 64, 131072),  # vec 8 only
+        (N.SoftmaxConfig(128, 8, C), 64, 8192),  # block below 256
+        (N.SoftmaxConfig(256, 8, C), 64, 200),  # 100 columns per CTA is not a multiple of 8
+        (N.SoftmaxConfig(256, 8, C), 2, 262144),  # more than 32 columns per thread over 8 CTAs
+    ]:
+        st, reason = N.validate("softmax", cfg, rows, cols)
+        assert st == N.KS_ERR_INVALID_CONFIG and "cluster" in reason, (cfg, rows, cols, reason)
+
+
 def test_validate_matmul(N):
     assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 8), 8192, 8192, 8192)[0] == 0
     st, reason = N.validate("matmul", N.MatmulConfig(128, 256, 64, 5, 2, 8), 64, 64, 64)

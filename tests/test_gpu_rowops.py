@@ -25,6 +25,13 @@ BLOCKS = (128, 256, 512, 1024)
 VECS = (1, 2, 4, 8)
 
 
+def MODES(N):
+    return (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS, N.KS_MODE_STAGED, N.KS_MODE_CLUSTER)
+
+
+CLUSTER_SHAPES = [(64, 131072), (256, 32768), (3, 16384), (2, 262144), (1000, 4096), (1, 16), (7, 48)]
+
+
 def _fx(family):
     return [p for p in fixture_paths() if os.path.basename(p).startswith(family + "_")]
 
@@ -44,7 +51,7 @@ def test_softmax_golden_all_configs(ks, path):
     r, c = fx["shape"]
     x = to_torch(fx["x"])
     ran = 0
-    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS, N.KS_MODE_STAGED)):
+    for block, vec, mode in itertools.product(BLOCKS, VECS, MODES(N)):
         cfg = N.SoftmaxConfig(block, vec, mode)
         st, _ = N.validate("softmax", cfg, r, c)
         if st != 0:
@@ -81,6 +88,23 @@ def test_softmax_warp_rows(ks, shape, block):
     assert_bf16_close(y, orf.softmax(inp["x"]))
 
 
+@pytest.mark.parametrize("shape", CLUSTER_SHAPES)
+@pytest.mark.parametrize("block", [256, 512, 1024])
+def test_softmax_cluster_rows(ks, shape, block):
+    """One row over a cluster of 2 to 8 CTAs: 1, 2 or 4 chunks per thread,
+    partly filled CTAs, and the max and sum combined through distributed
+    shared memory."""
+    N, ops = ks
+    cfg = N.SoftmaxConfig(block, 8, N.KS_MODE_CLUSTER)
+    st, reason = N.validate("softmax", cfg, *shape)
+    if st != 0:
+        assert "cluster" in reason
+        pytest.skip(reason)
+    inp = oin.generate_inputs("softmax", shape, seed=11)
+    y = to_numpy(ops.softmax(to_torch(inp["x"]), cfg=cfg))
+    assert_bf16_close(y, orf.softmax(inp["x"]))
+
+
 def test_softmax_rejects_bad_config(ks):
     N, ops = ks
     st, reason = N.validate("softmax", N.SoftmaxConfig(96, 8, 0), 4, 64)
@@ -102,7 +126,7 @@ def test_layernorm_golden_all_configs(ks, path):
     r, c = fx["shape"]
     x, g, b = (to_torch(fx[k]) for k in ("x", "gamma", "beta"))
     ran = 0
-    for block, vec, mode in itertools.product(BLOCKS, VECS, (N.KS_MODE_ONEPASS, N.KS_MODE_TWOPASS, N.KS_MODE_STAGED)):
+    for block, vec, mode in itertools.product(BLOCKS, VECS, MODES(N)):
         cfg = N.LayerNormConfig(block, vec, mode)
         if N.validate("layernorm", cfg, r, c)[0] != 0:
             continue
@@ -133,6 +157,20 @@ def test_layernorm_warp_rows(ks, shape, block):
     N, ops = ks
     inp = oin.generate_inputs("layernorm", shape, seed=10)
     cfg = N.LayerNormConfig(block, 8, N.KS_MODE_ONEPASS)
+    y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta")), cfg=cfg))
+    assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
+
+
+@pytest.mark.parametrize("shape", CLUSTER_SHAPES)
+@pytest.mark.parametrize("block", [256, 512, 1024])
+def test_layernorm_cluster_rows(ks, shape, block):
+    N, ops = ks
+    cfg = N.LayerNormConfig(block, 8, N.KS_MODE_CLUSTER)
+    st, reason = N.validate("layernorm", cfg, *shape)
+    if st != 0:
+        assert "cluster" in reason
+        pytest.skip(reason)
+    inp = oin.generate_inputs("layernorm", shape, seed=12)
     y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta")), cfg=cfg))
     assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
 

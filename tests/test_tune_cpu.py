@@ -42,10 +42,10 @@ def test_matmul_space():
 
 def test_rowop_spaces_and_rejections():
     sm = tune.query("enumerate", family="softmax", shape=[4096, 8192])
-    assert len(sm) == 18
+    assert len(sm) == 24
     rej = {v["symbol"]: v["reason"] for v in sm if not v["valid"]}
     assert "kernscope_b200_softmax_b128_v8_onepass" in rej and "registers" in rej["kernscope_b200_softmax_b128_v8_onepass"]
-    assert len(tune.query("enumerate", family="softmax", shape=[4096, 8192], full=True)) == 48
+    assert len(tune.query("enumerate", family="softmax", shape=[4096, 8192], full=True)) == 64
     red = tune.query("enumerate", family="reduction", shape=[1 << 28])
     assert all(v["valid"] for v in red)
     fa = tune.query("enumerate", family="flash_attention", shape=[8, 32, 8192, 128], causal=True)
@@ -103,15 +103,15 @@ def test_prescreen_only_run_and_cache_replay(tmp_path):
     cache = str(tmp_path / "c.json")
     rc, ev = tune.run(kernel_family="softmax", shape=[4096, 8192], arch="sm_100a", live_bench=False, cache=cache,
                       db=str(tmp_path / "db.jsonl"))
-    assert rc == 0 and ev["summary"]["variants_total"] == 18 and ev["summary"]["cached"] == 0
-    assert ev["summary"]["compiled"] + ev["summary"]["prescreen_rejected"] == 18
+    assert rc == 0 and ev["summary"]["variants_total"] == 24 and ev["summary"]["cached"] == 0
+    assert ev["summary"]["compiled"] + ev["summary"]["prescreen_rejected"] == 24
     c = json.load(open(cache))
     assert c["schema_version"] == 1
     (key, entry), = c["entries"].items()
     assert key == f"sm_100a:softmax:{fnv1a64('softmax:4096,8192')}"
-    assert entry["key"]["shape"] == [4096, 8192] and len(entry["configs"]) == 18
+    assert entry["key"]["shape"] == [4096, 8192] and len(entry["configs"]) == 24
     rc2, ev2 = tune.run(kernel_family="softmax", shape=[4096, 8192], arch="sm_100a", live_bench=False, cache=cache)
-    assert ev2["summary"]["cached"] == 18 and ev2["summary"]["compiled"] == 0
+    assert ev2["summary"]["cached"] == 24 and ev2["summary"]["compiled"] == 0
     # a different occupancy floor must not replay the cached outcomes
     rc3, ev3 = tune.run(kernel_family="softmax", shape=[4096, 8192], arch="sm_100a", live_bench=False, cache=cache,
                         min_occupancy=0.25)
