@@ -906,6 +906,10 @@ __global__ void bias_gelu_tail_kernel(const uint16_t *__restrict__ x, const uint
 // row in it has completed (its __syncthreads proves every thread has read
 // the slot into registers), so HBM reads never wait on the reductions.
 // Rows need cols % 8 == 0 (16-byte copies); chunks are 8 bf16 wide.
+// CTAs of up to 512 threads share an SM three ways and keep a 64 KB ring;
+// a 1024-thread CTA has the SM to itself and a ring of up to 200 KB, which
+// keeps two or three 64 KB rows in flight (layernorm then reads gamma and
+// beta through the L2 instead of holding them in the ring).
 // ===========================================================================
 constexpr int kMaxStages = 8;
 
@@ -932,8 +936,8 @@ KS_DEV void ring_drain(const RowRing &rg, int64_t i, int64_t my_rows, const KsWa
     ks_mbar_wait(rg.full + (j % rg.stages), uint32_t((j / rg.stages) & 1), nullptr, w);
 }
 
-template <int MAXCH>
-__global__ void __launch_bounds__(512) softmax_staged_kernel(const uint16_t *__restrict__ x,
+template <int MAXCH, int MAXT>
+__global__ void __launch_bounds__(MAXT) softmax_staged_kernel(const uint16_t *__restrict__ x,
                                                               uint16_t *__restrict__ y, int64_t rows,
                                                               int64_t cols, int stages, KsWait wait) {
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -974,8 +978,8 @@ __global__ void __launch_bounds__(512) softmax_staged_kernel(const uint16_t *__r
   if (threadIdx.x == 0 && i < my_rows) ring_drain(rg, i, my_rows, wait);
 }
 
-template <int MAXCH>
-__global__ void __launch_bounds__(512) layernorm_staged_kernel(const uint16_t *__restrict__ x,
+template <int MAXCH, int MAXT>
+__global__ void __launch_bounds__(MAXT) layernorm_staged_kernel(const uint16_t *__restrict__ x,
                                                                 const uint16_t *__restrict__ gamma,
                                                                 const uint16_t *__restrict__ beta,
                                                                 uint16_t *__restrict__ y, int64_t rows,
@@ -988,23 +992,29 @@ __global__ void __launch_bounds__(512) layernorm_staged_kernel(const uint16_t *_
   __shared__ int abort_flag;
   const int64_t my_rows = rows > blockIdx.x ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const uint32_t stride = uint32_t((cols * 2 + 127) & ~int64_t(127));
-  // slots [0, stages) hold rows; then gamma and beta
+  // slots [0, stages) hold rows; then gamma and beta (CTAs of up to 512
+  // threads) -- a 1024-thread CTA reads them from global memory
+  constexpr bool kGbShared = MAXT <= 512;
   RowRing rg{dsm, stride, uint32_t(cols * 2), stages, full};
-  const uint4 *g_s = reinterpret_cast<const uint4 *>(dsm + size_t(stages) * stride);
-  const uint4 *b_s = reinterpret_cast<const uint4 *>(dsm + size_t(stages + 1) * stride);
+  const uint4 *g_s = kGbShared ? reinterpret_cast<const uint4 *>(dsm + size_t(stages) * stride)
+                               : reinterpret_cast<const uint4 *>(gamma);
+  const uint4 *b_s = kGbShared ? reinterpret_cast<const uint4 *>(dsm + size_t(stages + 1) * stride)
+                               : reinterpret_cast<const uint4 *>(beta);
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) ks_mbar_init(full + s, 1);
     ks_mbar_init(&gb_full, 1);
     abort_flag = 0;
     ks_fence_mbar_init();
-    ks_mbar_arrive_expect_tx(&gb_full, 2 * uint32_t(cols * 2));
-    ks_bulk_load(dsm + size_t(stages) * stride, gamma, uint32_t(cols * 2), &gb_full);
-    ks_bulk_load(dsm + size_t(stages + 1) * stride, beta, uint32_t(cols * 2), &gb_full);
+    if (kGbShared) {
+      ks_mbar_arrive_expect_tx(&gb_full, 2 * uint32_t(cols * 2));
+      ks_bulk_load(dsm + size_t(stages) * stride, gamma, uint32_t(cols * 2), &gb_full);
+      ks_bulk_load(dsm + size_t(stages + 1) * stride, beta, uint32_t(cols * 2), &gb_full);
+    }
     for (int64_t i = 0; i < my_rows && i < stages; ++i) ring_issue(rg, x, cols, i);
   }
   __syncthreads();
   const int nvec = int(cols >> 3);
-  const bool gb_ok = ks_mbar_wait(&gb_full, 0, &abort_flag, wait);
+  const bool gb_ok = kGbShared ? ks_mbar_wait(&gb_full, 0, &abort_flag, wait) : true;
   int64_t i = 0;
   for (; i < my_rows && gb_ok; ++i) {
     const int s = int(i % stages);
@@ -1026,7 +1036,7 @@ __global__ void __launch_bounds__(512) layernorm_staged_kernel(const uint16_t *_
                           });
   }
   if (threadIdx.x == 0) {
-    if (!gb_ok) ks_mbar_wait(&gb_full, 0, nullptr, wait);
+    if (kGbShared && !gb_ok) ks_mbar_wait(&gb_full, 0, nullptr, wait);
     if (i < my_rows) ring_drain(rg, i, my_rows, wait);
   }
 }
@@ -1035,11 +1045,12 @@ __global__ void __launch_bounds__(512) layernorm_staged_kernel(const uint16_t *_
 // Host-side dispatch helpers
 // ---------------------------------------------------------------------------
 constexpr int kRegElems = 32;  // per-thread register budget for a ONEPASS row
-constexpr uint32_t kStagedRingBytes = 64 * 1024;  // row ring per CTA (3 CTAs fit an SM)
+constexpr uint32_t kStagedRingBytes = 64 * 1024;       // row ring per CTA (3 CTAs fit an SM)
+constexpr uint32_t kStagedRingBytesWide = 200 * 1024;  // 1024-thread CTAs, one per SM
 
-int staged_stages(int64_t cols) {
+int staged_stages(int64_t cols, int block) {
   const int64_t stride = (cols * 2 + 127) & ~int64_t(127);
-  int64_t s = kStagedRingBytes / stride;
+  int64_t s = (block == 1024 ? kStagedRingBytesWide : kStagedRingBytes) / stride;
   if (s > kMaxStages) s = kMaxStages;
   return int(s);
 }
@@ -1144,11 +1155,11 @@ int rowop_validate(const char *fam, int block, int vec, int mode, int64_t rows, 
                    fam, (long long)cols, (long long)(int64_t(block) * 32 * 8));
     return KS_ERR_INVALID_CONFIG;
   }
-  if (mode == KS_MODE_STAGED && (vec != 8 || block > 512 || staged_stages(cols) < 2)) {
+  if (mode == KS_MODE_STAGED && (vec != 8 || staged_stages(cols, block) < 2)) {
     ks::set_reason(reason, len,
-                   "%s: staged copies whole rows with 16-byte bulk copies: vec_width must be 8, block <= 512 "
-                   "and a two-row ring must fit %u bytes (cols %lld)",
-                   fam, kStagedRingBytes, (long long)cols);
+                   "%s: staged copies whole rows with 16-byte bulk copies: vec_width must be 8 and a two-row "
+                   "ring must fit %u bytes (%u at block 1024; cols %lld)",
+                   fam, kStagedRingBytes, kStagedRingBytesWide, (long long)cols);
     return KS_ERR_INVALID_CONFIG;
   }
   ks::set_reason(reason, len, "");
@@ -1173,9 +1184,9 @@ int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, c
     }
   } else if (cfg.mode == KS_MODE_STAGED) {
     if constexpr (VEC == 8) {
-      const int stages = staged_stages(a.cols);
+      const int stages = staged_stages(a.cols, cfg.block);
       const size_t shm = size_t(stages) * size_t((a.cols * 2 + 127) & ~int64_t(127));
-      auto k = softmax_staged_kernel<kRegElems / 8>;
+      auto k = cfg.block == 1024 ? softmax_staged_kernel<kRegElems / 8, 1024> : softmax_staged_kernel<kRegElems / 8, 512>;
       cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shm));
       if (e != cudaSuccess) return ks::map_cuda(e);
       k<<<grid_for(k, cfg.block, a.rows, shm), cfg.block, shm, st>>>(x, y, a.rows, a.cols, stages, ks::wait_ctx());
@@ -1230,9 +1241,10 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
     }
   } else if (cfg.mode == KS_MODE_STAGED) {
     if constexpr (VEC == 8) {
-      const int stages = staged_stages(a.cols);
-      const size_t shm = size_t(stages + 2) * size_t((a.cols * 2 + 127) & ~int64_t(127));
-      auto k = layernorm_staged_kernel<kRegElems / 8>;
+      const bool wide = cfg.block == 1024;
+      const int stages = staged_stages(a.cols, cfg.block);
+      const size_t shm = size_t(stages + (wide ? 0 : 2)) * size_t((a.cols * 2 + 127) & ~int64_t(127));
+      auto k = wide ? layernorm_staged_kernel<kRegElems / 8, 1024> : layernorm_staged_kernel<kRegElems / 8, 512>;
       cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shm));
       if (e != cudaSuccess) return ks::map_cuda(e);
       k<<<grid_for(k, cfg.block, a.rows, shm), cfg.block, shm, st>>>(x, g, b, y, a.rows, a.cols,

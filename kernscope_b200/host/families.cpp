@@ -790,10 +790,13 @@ class RowFamily : public Family {
       res.regs_per_thread = 50;  // up to four 8-wide chunks per thread
       res.smem_bytes = 288;      // warp partials and the cluster slots
     } else if (mode == KS_MODE_STAGED) {
+      // 64 KB ring (plus gamma/beta for layernorm) up to 512 threads; a
+      // 1024-thread CTA keeps a 200 KB ring and reads gamma/beta from L2
+      const bool wide = block == 1024;
       const std::int64_t stride = (c * 2 + 127) / 128 * 128;
-      const int stages = int(std::min<std::int64_t>(8, 65536 / std::max<std::int64_t>(stride, 1)));
-      res.smem_bytes = int(stride * (stages + (kind == RowKind::kLayerNorm ? 2 : 0))) + 512;
-      res.regs_per_thread = 80;
+      const int stages = int(std::min<std::int64_t>(8, (wide ? 204800 : 65536) / std::max<std::int64_t>(stride, 1)));
+      res.smem_bytes = int(stride * (stages + (kind == RowKind::kLayerNorm && !wide ? 2 : 0))) + 512;
+      res.regs_per_thread = wide ? 64 : 80;
     } else if (iget(cfg, "vec_width", 8) == 8 && mode == KS_MODE_ONEPASS && c <= 1024 &&
                (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm)) {
       // one row per warp, at most 256 threads per CTA; layernorm also keeps

@@ -105,6 +105,21 @@ def test_softmax_cluster_rows(ks, shape, block):
     assert_bf16_close(y, orf.softmax(inp["x"]))
 
 
+STAGED_WIDE_SHAPES = [(300, 32768), (5, 16384), (1000, 4096), (149, 24576)]
+
+
+@pytest.mark.parametrize("shape", STAGED_WIDE_SHAPES)
+def test_softmax_staged_wide(ks, shape):
+    """1024-thread STAGED CTAs: a 200 KB ring of up to 8 rows, three 64 KB
+    rows at 32768 columns, more rows than CTAs."""
+    N, ops = ks
+    cfg = N.SoftmaxConfig(1024, 8, N.KS_MODE_STAGED)
+    assert N.validate("softmax", cfg, *shape)[0] == 0
+    inp = oin.generate_inputs("softmax", shape, seed=13)
+    y = to_numpy(ops.softmax(to_torch(inp["x"]), cfg=cfg))
+    assert_bf16_close(y, orf.softmax(inp["x"]))
+
+
 def test_softmax_rejects_bad_config(ks):
     N, ops = ks
     st, reason = N.validate("softmax", N.SoftmaxConfig(96, 8, 0), 4, 64)
@@ -171,6 +186,17 @@ def test_layernorm_cluster_rows(ks, shape, block):
         assert "cluster" in reason
         pytest.skip(reason)
     inp = oin.generate_inputs("layernorm", shape, seed=12)
+    y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta")), cfg=cfg))
+    assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
+
+
+@pytest.mark.parametrize("shape", STAGED_WIDE_SHAPES)
+def test_layernorm_staged_wide(ks, shape):
+    """1024-thread STAGED CTAs read gamma and beta from global memory."""
+    N, ops = ks
+    cfg = N.LayerNormConfig(1024, 8, N.KS_MODE_STAGED)
+    assert N.validate("layernorm", cfg, *shape)[0] == 0
+    inp = oin.generate_inputs("layernorm", shape, seed=14)
     y = to_numpy(ops.layernorm(*(to_torch(inp[k]) for k in ("x", "gamma", "beta")), cfg=cfg))
     assert_bf16_close(y, orf.layernorm(inp["x"], inp["gamma"], inp["beta"]))
 
