@@ -41,7 +41,7 @@ def test_softmax_pipeline_gate_injection_and_cache(tune, tmp_path):
     rc, ev = tune.run(inject_gate_failure=2, **opts)
     assert rc == 0 and ev["status"] == "ok" and ev["live"]
     s = ev["summary"]
-    assert s["variants_total"] == 18 and s["prescreen_rejected"] >= 1
+    assert s["variants_total"] == 24 and s["prescreen_rejected"] >= 1
     assert s["golden_gate_failed"] == 1  # exactly the injected variant
     failed = [v for v in ev["variants"] if v["status"] == "golden_gate_failed"]
     assert len(failed) == 1 and "golden gate failed" in failed[0]["reason"]
@@ -56,7 +56,7 @@ def test_softmax_pipeline_gate_injection_and_cache(tune, tmp_path):
     assert q["best"]["config"] == ev["best"]["config"]
     # second run: everything replayed from the tunecache, nothing launched
     rc2, ev2 = tune.run(**opts)
-    assert rc2 == 0 and ev2["summary"]["cached"] == 18 and ev2["summary"]["compiled"] == 0
+    assert rc2 == 0 and ev2["summary"]["cached"] == 24 and ev2["summary"]["compiled"] == 0
     assert ev2["best"]["config"] == ev["best"]["config"]
 
 
