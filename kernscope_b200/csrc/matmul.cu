@@ -64,7 +64,7 @@ KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
+                     uint16_t *__restrict__ c, int M, int N, int K, int group_m, int b3d, KsWait wait) {
   using L = MmLayout<BN, STAGES, ACC>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
@@ -125,9 +125,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
         ks_mbar_arrive_expect_tx(full + stage, kABytes + L::b_bytes);
         ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
+        if (b3d) {
+          // one copy for all BN/64 column blocks (tensor map dims: 64 columns, K, N/64)
+          ks_tma_load_3d(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64));
+        } else {
 #pragma unroll
-        for (int j = 0; j < BN / 64; ++j)
-          ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+          for (int j = 0; j < BN / 64; ++j)
+            ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+        }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) {
@@ -512,9 +517,18 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   int s = ks::encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, uint64_t(a.k), uint64_t(a.m),
                              uint64_t(a.k) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != KS_OK) return s;
-  s = ks::encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, uint64_t(a.n), uint64_t(a.k),
-                         uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (s != KS_OK) return s;
+  // B as (64 columns, K, N/64 column blocks) when N is a multiple of 64, so
+  // one copy per stage fetches all BN/64 blocks; else one 2-D box per block.
+  int b3d = 0;
+  if (BN > 64 && a.n % 64 == 0 &&
+      ks::encode_tmap_3d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, 64, uint64_t(a.k), uint64_t(a.n / 64),
+                         uint64_t(a.n) * 2, 128, 64, kBK, BN / 64, CU_TENSOR_MAP_SWIZZLE_128B) == KS_OK)
+    b3d = 1;
+  if (!b3d) {
+    s = ks::encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, uint64_t(a.n), uint64_t(a.k),
+                           uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KS_OK) return s;
+  }
   auto kern = matmul_tc_kernel<BN, STAGES, ACC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
@@ -522,7 +536,7 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   const int sms = ks::sm_count();
   const int grid = int(tiles < sms ? tiles : sms);
   kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n),
-                                                int(a.k), cfg.group_m, ks::wait_ctx());
+                                                int(a.k), cfg.group_m, b3d, ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
 
