@@ -105,7 +105,8 @@ typedef enum ks_dtype { KS_BF16 = 0, KS_F32 = 1, KS_F64 = 2 } ks_dtype;
  * re-read for the second statistic (second read served by L2), which lifts
  * the register cap on the row length.  STAGED (softmax, layernorm): a ring
  * of whole rows in shared memory filled by bulk copies keeps several rows
- * per CTA in flight (vec_width 8, cols % 8 == 0, cols <= 16384). */
+ * per CTA in flight (vec_width 8, cols % 8 == 0; a 64 KB ring up to 512
+ * threads, cols <= 16384; a 200 KB ring at 1024 threads, cols <= 32768). */
 typedef enum ks_elem_mode {
   KS_MODE_ONEPASS = 0,
   KS_MODE_TWOPASS = 1,
@@ -122,7 +123,8 @@ typedef enum ks_elem_mode {
  * Reference kernel arguments: (x, out, rows, cols).
  * cfg.block: threads per row-CTA {128,256,512,1024};
  * cfg.vec_width: bf16 per vector access {1,2,4,8} (8 = 128-bit);
- * cfg.mode: KS_MODE_ONEPASS | KS_MODE_TWOPASS.                             */
+ * cfg.mode: KS_MODE_ONEPASS | KS_MODE_TWOPASS | KS_MODE_STAGED |
+ *           KS_MODE_CLUSTER (the same modes apply to layernorm).           */
 typedef struct ks_softmax_config { int block; int vec_width; int mode; } ks_softmax_config;
 typedef struct ks_softmax_args {
   const void *x; void *out; int64_t rows; int64_t cols;
