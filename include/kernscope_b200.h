@@ -194,8 +194,10 @@ int ks_reduction_launch(const ks_reduction_config *cfg, const ks_reduction_args 
  * library-owned static device array of KS_REDUCTION_NOALLOC_SCRATCH_BYTES,
  * held on every GPU that loads the library until the process exits.
  * Returns KS_ERR_WORKSPACE when ks_reduction_workspace_bytes() for these
- * args exceeds that size.  The first call on each device resolves the
- * array's device address (do it before any stream capture).  All calls
+ * args exceeds that size.  The first call in each driver context (normally
+ * a device's primary context) resolves the array's device address (do it
+ * before any stream capture); cudaDeviceReset destroys the array with the
+ * context, so do not call this again after a reset in the same process.  All calls
  * share the array: calls that overlap on the GPU race and must be
  * serialised by the caller.  Allocates nothing.                            */
 #define KS_REDUCTION_NOALLOC_SCRATCH_BYTES (1u << 20)

@@ -16,13 +16,21 @@
 * ``kernscope_b200/lib/ks-template-runner`` -- runs one kernel on raw host
   buffers (the gate runner of the reference's template flow).
 
-Objects are rebuilt only when a source or header is newer than the object.
+Every output is rebuilt when the content hash of its inputs changes: the
+sources, the headers, the compiler's version line and the exact command line
+(flags included).  The hash sits in a ``.stamp`` file beside each output, so
+a prebuilt tree whose stamps do not match the sources is rebuilt whatever
+the files' mtimes say.  The kernel library also carries the hash of its
+sources and flags in ``ks_build_info()`` ("src <hex>"), which
+``source_hash()`` recomputes: a loaded library that reports another hash was
+not built from these sources.
 """
 
 from __future__ import annotations
 
 import argparse
 import glob
+import hashlib
 import os
 import subprocess
 import sys
@@ -45,11 +53,67 @@ BENCH_CLI = os.path.join(LIBDIR, "kernscope-bench")
 RUNNER_CLI = os.path.join(LIBDIR, "ks-template-runner")
 
 
-def _newer(target: str, deps) -> bool:
-    if not os.path.exists(target):
+def _digest(parts) -> str:
+    h = hashlib.sha256()
+    for p in parts:
+        h.update(p if isinstance(p, bytes) else str(p).encode())
+        h.update(b"\0")
+    return h.hexdigest()
+
+
+def _file_digest(paths) -> str:
+    parts = []
+    for p in paths:
+        parts.append(os.path.relpath(p, ROOT))
+        with open(p, "rb") as fh:
+            parts.append(fh.read())
+    return _digest(parts)
+
+
+_VERSIONS: dict = {}
+
+
+def _tool_version(tool: str) -> str:
+    if tool not in _VERSIONS:
+        try:
+            r = subprocess.run([tool, "--version"], capture_output=True, text=True)
+            _VERSIONS[tool] = r.stdout.strip().splitlines()[-1] if r.stdout.strip() else tool
+        except OSError:
+            _VERSIONS[tool] = tool
+    return _VERSIONS[tool]
+
+
+def _stale(target: str, key: str) -> bool:
+    """True unless `target` exists and its stamp records `key`."""
+    stamp = target + ".stamp"
+    if not os.path.exists(target) or not os.path.exists(stamp):
         return True
-    t = os.path.getmtime(target)
-    return any(os.path.getmtime(d) > t for d in deps)
+    with open(stamp) as fh:
+        return fh.read().strip() != key
+
+
+def _stamp(target: str, key: str) -> None:
+    with open(target + ".stamp", "w") as fh:
+        fh.write(key + "\n")
+
+
+def _kernel_sources():
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    hdrs = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INCLUDE, "kernscope_b200.h")]
+    return srcs, hdrs
+
+
+def _compile_flags():
+    return [*GENCODE, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-rdc=false", "-I", INCLUDE,
+            "-I", CSRC]
+
+
+def source_hash() -> str:
+    """Hash of the kernel library's sources, headers, nvcc flags and nvcc
+    version: the value the library built from them reports in
+    ``ks_build_info()``."""
+    srcs, hdrs = _kernel_sources()
+    return _digest([_file_digest(srcs + hdrs), " ".join(_compile_flags()), _tool_version(NVCC)])[:16]
 
 
 def _run(cmd):
@@ -62,26 +126,37 @@ def _run(cmd):
 def build_kernels(jobs: int, force: bool, verbose_ptxas: bool = False) -> str:
     os.makedirs(LIBDIR, exist_ok=True)
     os.makedirs(OBJDIR, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    hdrs = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INCLUDE, "kernscope_b200.h")]
-    objs = []
-    cmds = []
+    srcs, hdrs = _kernel_sources()
+    src_hash = source_hash()
+    hdr_digest = _file_digest(hdrs)
+    objs, keys, cmds = [], [], []
     for s in srcs:
         o = os.path.join(OBJDIR, os.path.basename(s) + ".o")
+        cmd = [NVCC, *_compile_flags(), f"-DKS_SOURCE_HASH=\"{src_hash}\"", "-c", s, "-o", o]
+        key = _digest([_file_digest([s]), hdr_digest, " ".join(cmd), _tool_version(NVCC)])
         objs.append(o)
-        if force or _newer(o, [s] + hdrs):
-            cmd = [NVCC, *GENCODE, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
-                   "-rdc=false", "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o]
+        keys.append(key)
+        if force or _stale(o, key):
             if verbose_ptxas:
                 cmd.insert(1, "-Xptxas=-v")
-            cmds.append(cmd)
+            cmds.append((cmd, o, key))
     log = []
+
+    def one(job):
+        cmd, o, key = job
+        out = _run(cmd)
+        _stamp(o, key)
+        return out
+
     with ThreadPoolExecutor(max_workers=max(1, jobs)) as ex:
-        for out in ex.map(_run, cmds):
+        for out in ex.map(one, cmds):
             log.append(out)
-    if force or cmds or _newer(KERNEL_LIB, objs):
-        _run([NVCC, *GENCODE, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", *objs,
-              "-o", KERNEL_LIB, "-ldl", "-lpthread", "-lrt"])
+    link = [NVCC, *GENCODE, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", *objs, "-o", KERNEL_LIB, "-ldl",
+            "-lpthread", "-lrt"]
+    lkey = _digest([*keys, " ".join(link)])
+    if force or cmds or _stale(KERNEL_LIB, lkey):
+        _run(link)
+        _stamp(KERNEL_LIB, lkey)
     return "\n".join(log)
 
 
@@ -101,13 +176,24 @@ def build_tuner(force: bool) -> None:
     cxx = os.environ.get("KS_CXX", "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++")
     common = ["-std=c++20", "-O2", "-fPIC", "-Wall", "-I", INCLUDE, "-I", HOST]
     rpath = "-Wl,-rpath,$ORIGIN"
-    if force or _newer(TUNE_LIB, lib_srcs + hdrs + [KERNEL_LIB]):
-        _run([cxx, *common, "-shared", *lib_srcs, "-o", TUNE_LIB, "-L", LIBDIR, "-lkernscope_b200",
-              rpath, "-ldl", "-lpthread"])
+    hdr_digest = _file_digest(hdrs)
+    with open(KERNEL_LIB + ".stamp") as fh:
+        kernel_key = fh.read().strip()
+    lib_cmd = [cxx, *common, "-shared", *lib_srcs, "-o", TUNE_LIB, "-L", LIBDIR, "-lkernscope_b200", rpath, "-ldl",
+               "-lpthread"]
+    lib_key = _digest([_file_digest(lib_srcs), hdr_digest, kernel_key, " ".join(lib_cmd), _tool_version(cxx)])
+    if force or _stale(TUNE_LIB, lib_key):
+        _run(lib_cmd)
+        _stamp(TUNE_LIB, lib_key)
     for src, out in ((cli_src, TUNE_CLI), (bench_src, BENCH_CLI), (runner_src, RUNNER_CLI)):
-        if src and (force or _newer(out, src + hdrs + [TUNE_LIB])):
-            _run([cxx, *common, *src, "-o", out, "-L", LIBDIR, "-lkernscope_tune", "-lkernscope_b200",
-                  rpath, "-ldl", "-lpthread"])
+        if not src:
+            continue
+        cmd = [cxx, *common, *src, "-o", out, "-L", LIBDIR, "-lkernscope_tune", "-lkernscope_b200", rpath, "-ldl",
+               "-lpthread"]
+        key = _digest([_file_digest(src), hdr_digest, lib_key, " ".join(cmd), _tool_version(cxx)])
+        if force or _stale(out, key):
+            _run(cmd)
+            _stamp(out, key)
 
 
 def build(jobs: int = 8, force: bool = False, verbose_ptxas: bool = False) -> str:

@@ -389,6 +389,10 @@ int encode_tmap_3d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uin
                    uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
                    CUtensorMapSwizzle swz);
 int sm_count();
+// Device address of a __device__ variable of this library in the driver
+// context current on this thread, resolved once per (context, symbol) with
+// cudaGetSymbolAddress and cached.
+int symbol_address(const void *symbol, void **out);
 // Wait settings for kernels launched on the current device (error word
 // address resolved once per device, limit from ks_set_wait_limit_ns).
 KsWait wait_ctx();

@@ -257,7 +257,7 @@ int plan(const ks_reduction_config &c, const ks_reduction_args &a, Plan &p, char
                    (long long)a.rows, (long long)a.cols);
     return KS_ERR_INVALID_ARGS;
   }
-  const int sms = 148;  // planning constant: a B200 has 148 SMs
+  const int sms = ks::sm_count();  // the current device's SMs (148 on a B200, and without a device)
   if (a.axis == -1) {
     if (a.in_dtype != KS_F32 || a.out_dtype != KS_F32) {
       ks::set_reason(reason, len, "reduction: the full sum (axis -1) takes fp32 in and fp32 out");
@@ -417,9 +417,12 @@ int ks_reduction_launch(const ks_reduction_config *cfg, const ks_reduction_args 
 //   the process exits.  Launches whose workspace would be larger return
 //   KS_ERR_WORKSPACE.
 // * Host code cannot use the array's name as a device address (it names a
-//   host-side shadow).  The first call on each device resolves the address
-//   with cudaGetSymbolAddress while that device is current and caches it;
-//   make that first call before any stream capture.
+//   host-side shadow).  The first call in each driver context (normally a
+//   device's primary context) resolves the address with cudaGetSymbolAddress
+//   while that device is current and caches it per context; make that first
+//   call before any stream capture.  cudaDeviceReset destroys the context and
+//   the array with it: do not call this entry point again after a reset in
+//   the same process.
 // * Every call shares the one array and it keeps the last call's contents;
 //   the launch clears the arrival counters it needs on the stream before the
 //   kernel.  Calls that overlap on the GPU (concurrent streams, several host
@@ -433,36 +436,17 @@ static_assert(kReductionNoallocScratchBytes == KS_REDUCTION_NOALLOC_SCRATCH_BYTE
 
 static __device__ __align__(256) unsigned char g_reduction_scratch[kReductionNoallocScratchBytes];
 
-int noalloc_scratch_address(void **out) {
-  constexpr int kMaxDevices = 64;
-  static void *addr[kMaxDevices] = {};
-  static std::mutex mu;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return ks::map_cuda(e);
-  if (dev < 0 || dev >= kMaxDevices) return KS_ERR_DEVICE_NOT_FOUND;
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_reduction_scratch);
-    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? ks::map_cuda(e) : KS_ERR_OTHER;
-    addr[dev] = p;
-  }
-  *out = addr[dev];
-  return KS_OK;
-}
-
 }  // namespace
 
 extern "C" int ks_reduction_launch_noalloc(const ks_reduction_config *cfg, const ks_reduction_args *args,
                                            void *stream) {
-  if (!cfg || !args) return KS_ERR_INVALID_ARGS;
+  if (!cfg || !args || !args->x || !args->out) return KS_ERR_INVALID_ARGS;  // before any CUDA call
   size_t need = 0;
   int s = ks_reduction_workspace_bytes(cfg, args, &need);
   if (s != KS_OK) return s;
   if (need > kReductionNoallocScratchBytes) return KS_ERR_WORKSPACE;
   void *scratch = nullptr;
-  if ((s = noalloc_scratch_address(&scratch)) != KS_OK) return s;
+  if ((s = ks::symbol_address(reinterpret_cast<const void *>(&g_reduction_scratch), &scratch)) != KS_OK) return s;
   ks_reduction_args a = *args;
   a.workspace = scratch;
   a.workspace_bytes = kReductionNoallocScratchBytes;

@@ -1074,6 +1074,11 @@ int grid_for(K kernel, int block, int64_t work, size_t dyn_smem = 0) {
 // would hold more than 4 chunks per lane and cost the occupancy that keeps
 // rows in flight.
 constexpr int64_t kWarpRowCols = 1024;
+// The 8-wide ONEPASS kernels index rows with int and step by the resident
+// grid (r + stride, stride = CTAs x rows per CTA < 2^30), so they take fewer
+// than 2^30 rows; r + stride then stays below 2^31.  Larger row counts run
+// the int64 generic kernels.
+constexpr int64_t kIntRows = int64_t(1) << 30;
 // 16-byte chunks per lane for a warp-held row: 1, 2 or 4.
 int warp_chunks(int64_t cols) {
   const int64_t per_lane = (cols / 8 + 31) / 32;
@@ -1096,7 +1101,8 @@ int cluster_plan(int block, int64_t rows, int64_t cols) {
   if (cols % 8 != 0 || block < 256) return 0;
   int cs = 2;
   while (cs < 8 && cols > int64_t(block) * 16 * cs) cs <<= 1;
-  while (cs < 8 && rows * cs < 2 * 148 && cols % (int64_t(cs) * 16) == 0 && cols / (cs * 2) >= int64_t(block) * 8)
+  const int64_t sms = ks::sm_count();
+  while (cs < 8 && rows * cs < 2 * sms && cols % (int64_t(cs) * 16) == 0 && cols / (cs * 2) >= int64_t(block) * 8)
     cs <<= 1;
   if (cols % (int64_t(cs) * 8) != 0 || cols > int64_t(block) * 32 * cs) return 0;
   return cs;
@@ -1196,7 +1202,7 @@ int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, c
   } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = softmax_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, y, a.rows, a.cols);
-  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < (int64_t(1) << 31)) {
+  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < kIntRows) {
     const int block = cfg.block < 256 ? cfg.block : 256;
     switch (warp_chunks(a.cols)) {
       case 1: return launch_rows_warp(softmax_warp_v8_kernel<1>, block, a.rows, st, x, y, int(a.rows), int(a.cols));
@@ -1204,7 +1210,7 @@ int launch_softmax_vec(const ks_softmax_config &cfg, const ks_softmax_args &a, c
       default:
         return launch_rows_warp(softmax_warp_v8_kernel<4>, block, a.rows, st, x, y, int(a.rows), int(a.cols));
     }
-  } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
+  } else if (VEC == 8 && a.rows < kIntRows && a.cols < (int64_t(1) << 31)) {
     auto k = cfg.block <= 256 ? softmax_onepass_v8_kernel<kRegElems / 8, 256>
                               : softmax_onepass_v8_kernel<kRegElems / 8, 1024>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, y, int(a.rows), int(a.cols));
@@ -1256,7 +1262,7 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
   } else if (cfg.mode == KS_MODE_TWOPASS) {
     auto k = layernorm_twopass_kernel<VEC>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, g, b, y, a.rows, a.cols, eps);
-  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < (int64_t(1) << 31)) {
+  } else if (VEC == 8 && a.cols <= kWarpRowCols && a.rows < kIntRows) {
     const int block = cfg.block < 256 ? cfg.block : 256;
     const float ic = 1.f / float(a.cols);
     switch (warp_chunks(a.cols)) {
@@ -1270,7 +1276,7 @@ int launch_layernorm_vec(const ks_layernorm_config &cfg, const ks_layernorm_args
         return launch_rows_warp(layernorm_warp_v8_kernel<4>, block, a.rows, st, x, g, b, y, int(a.rows), int(a.cols),
                                 ic, eps);
     }
-  } else if (VEC == 8 && a.rows < (int64_t(1) << 31) && a.cols < (int64_t(1) << 31)) {
+  } else if (VEC == 8 && a.rows < kIntRows && a.cols < (int64_t(1) << 31)) {
     auto k = cfg.block <= 256 ? layernorm_onepass_v8_kernel<kRegElems / 8, 256>
                               : layernorm_onepass_v8_kernel<kRegElems / 8, 1024>;
     k<<<grid_for(k, cfg.block, a.rows), cfg.block, 0, st>>>(x, g, b, y, int(a.rows), int(a.cols),

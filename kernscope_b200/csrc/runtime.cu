@@ -10,6 +10,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <vector>
 
 #include "ks_common.cuh"
 
@@ -45,19 +46,63 @@ int check_arch_sm100() {
   return major == 10 ? KS_OK : KS_ERR_ARCH;
 }
 
-KsWait wait_ctx() {
-  constexpr int kMaxDev = 64;
-  static int *addr[kMaxDev] = {};
+// The driver context current on this thread (cuCtxGetCurrent, reached through
+// the runtime's driver entry point so that the library needs no libcuda link);
+// nullptr when the driver does not answer.
+static void *current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+int symbol_address(const void *symbol, void **out) {
+  // A __device__ variable's address belongs to the module as loaded in one
+  // driver context, so the cache is keyed on (context, symbol): a second
+  // context on the same device (cuCtxCreate) resolves its own address.
+  struct Entry { void *ctx; const void *sym; void *addr; };
+  static std::vector<Entry> cache;
   static std::mutex mu;
   int dev = 0;
-  KsWait w{nullptr, g_wait_limit_ns.load()};
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return w;
-  std::lock_guard<std::mutex> lk(mu);
-  if (addr[dev] == nullptr) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_ks_device_error) == cudaSuccess) addr[dev] = static_cast<int *>(p);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return map_cuda(e);
+  void *ctx = current_context();
+  if (ctx == nullptr) {
+    // no context is current on this thread yet: cudaSetDevice makes the
+    // device's primary context current (CUDA 12 initialises it there), the
+    // one the launches will then use
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return map_cuda(e);
+    ctx = current_context();
+    if (ctx == nullptr) return KS_ERR_NO_DRIVER;
   }
-  w.err = addr[dev];
+  std::lock_guard<std::mutex> lk(mu);
+  for (const Entry &x : cache)
+    if (x.ctx == ctx && x.sym == symbol) {
+      *out = x.addr;
+      return KS_OK;
+    }
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, symbol);
+  if (e != cudaSuccess) return map_cuda(e);
+  if (p == nullptr) return KS_ERR_OTHER;
+  cache.push_back({ctx, symbol, p});
+  *out = p;
+  return KS_OK;
+}
+
+KsWait wait_ctx() {
+  KsWait w{nullptr, g_wait_limit_ns.load()};
+  void *p = nullptr;
+  if (symbol_address(reinterpret_cast<const void *>(&g_ks_device_error), &p) == KS_OK) w.err = static_cast<int *>(p);
   return w;
 }
 
@@ -169,7 +214,12 @@ const char *ks_status_string(int s) {
 }
 
 int ks_abi_version(void) { return KS_ABI_VERSION; }
-const char *ks_build_info(void) { return "kernscope_b200 sm_100a nvcc " __DATE__; }
+#ifndef KS_SOURCE_HASH
+#define KS_SOURCE_HASH "unknown"
+#endif
+// "src <hash>": the hash of the sources, headers, flags and nvcc version this
+// library was compiled from (kernscope_b200/build.py: source_hash()).
+const char *ks_build_info(void) { return "kernscope_b200 sm_100a nvcc src " KS_SOURCE_HASH; }
 
 int ks_gpu_device_count(int *count) {
   if (!count) return KS_ERR_INVALID_ARGS;

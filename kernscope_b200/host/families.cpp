@@ -92,6 +92,14 @@ int download_bf16(const DevBuf &d, size_t n, std::vector<float> *out) {
 
 int iget(const json &c, const char *k, int d) { return int(c.number_or(k, d)); }
 
+// SMs of the current device, as the launches see them (ks_gpu_sm_count); the
+// sm_100a model's count when no device answers (pre-screen without a GPU).
+std::int64_t device_sms() {
+  int dev = 0, n = 0;
+  if (ks_gpu_get_device(&dev) == KS_OK && ks_gpu_sm_count(dev, &n) == KS_OK && n > 0) return n;
+  return get_arch("sm_100a").sm_count;
+}
+
 std::string shape_str(const std::vector<std::int64_t> &s) {
   std::string o;
   for (size_t i = 0; i < s.size(); ++i) o += (i ? "," : "") + std::to_string(s[i]);
@@ -123,7 +131,8 @@ int mode_from(const json &c, int dflt) {
 std::int64_t cluster_ctas(int block, std::int64_t rows, std::int64_t cols) {
   std::int64_t cs = 2;
   while (cs < 8 && cols > std::int64_t(block) * 16 * cs) cs <<= 1;
-  while (cs < 8 && rows * cs < 2 * 148 && cols % (cs * 16) == 0 && cols / (cs * 2) >= std::int64_t(block) * 8)
+  const std::int64_t sms = device_sms();
+  while (cs < 8 && rows * cs < 2 * sms && cols % (cs * 16) == 0 && cols / (cs * 2) >= std::int64_t(block) * 8)
     cs <<= 1;
   return cs;
 }
@@ -816,7 +825,7 @@ class RowFamily : public Family {
     const Resources res = resources(cfg, s);
     const auto occ = occupancy::compute_occupancy(get_arch("sm_100a"), res.regs_per_thread, res.smem_bytes,
                                                   g.block_x, 0);
-    const std::int64_t cap = std::int64_t(std::max(1, occ.blocks_per_sm)) * 148;
+    const std::int64_t cap = std::int64_t(std::max(1, occ.blocks_per_sm)) * device_sms();
     if (kind == RowKind::kBiasGelu) {
       const std::int64_t nvec = c / std::max(1, iget(cfg, "vec_width", 8));
       g.grid_x = int((nvec + g.block_x - 1) / g.block_x);
@@ -999,7 +1008,8 @@ LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) no
   LaunchGeometry g;
   const std::int64_t tiles = ((p.m + c.tile_m - 1) / c.tile_m) * ((p.n + c.tile_n - 1) / c.tile_n);
   // persistent: one CTA per SM (tile_m 256: one CTA pair per two SMs)
-  g.grid_x = c.tile_m == 256 ? int(2 * std::min<std::int64_t>(tiles, 74)) : int(std::min<std::int64_t>(tiles, 148));
+  const std::int64_t sms = device_sms();
+  g.grid_x = c.tile_m == 256 ? int(2 * std::min<std::int64_t>(tiles, sms / 2)) : int(std::min<std::int64_t>(tiles, sms));
   g.block_x = 192;
   g.smem_bytes = int(smem_bytes(c));
   g.tmem_columns = pow2_cols(c.acc_stages * c.tile_n);
@@ -1011,7 +1021,7 @@ LaunchGeometry launch_geometry(const FlashAttentionConfig &c, const FlashAttenti
   g.grid_x = int((p.nq + c.tile_m - 1) / c.tile_m);
   g.grid_y = int(p.batch_heads);
   if (c.tile_m == 256) {  // persistent: one CTA per SM over the (query block, head) items
-    g.grid_x = int(std::min<std::int64_t>(std::int64_t(g.grid_x) * g.grid_y, 148));
+    g.grid_x = int(std::min<std::int64_t>(std::int64_t(g.grid_x) * g.grid_y, device_sms()));
     g.grid_y = 1;
   }
   const bool tc = fa_tensor_path(c, p.d);

@@ -41,6 +41,14 @@ def test_abi_version_and_status(N):
     assert N.status_string(-5) == "launch_failed"  # GpuError::kLaunchFailed
 
 
+def test_library_built_from_these_sources(N):
+    """The loaded library reports the hash of the sources, headers, nvcc flags
+    and nvcc version it was compiled from; it must be this tree's."""
+    from kernscope_b200 import build
+
+    assert f"src {build.source_hash()}" in N.lib.ks_build_info().decode()
+
+
 def test_validate_rowops(N):
     assert N.validate("softmax", N.SoftmaxConfig(256, 8, 0), 4096, 8192) == (0, "")
     st, reason = N.validate("softmax", N.SoftmaxConfig(128, 8, 0), 4096, 8192)
@@ -105,6 +113,8 @@ def _launch_cases(N):
         ("ks_layernorm_launch", N.LayerNormConfig(128, 8, 0), N.LayerNormArgs(None, None, None, None, 64, 64, 1e-5)),
         ("ks_bias_gelu_launch", N.BiasGeluConfig(128, 8, 1), N.BiasGeluArgs(None, None, None, 64 * 64, 64)),
         ("ks_reduction_launch", N.ReductionConfig(256, 4, 2),
+         N.ReductionArgs(None, None, 64, 64, 0, 0, 0, None, 0, None)),
+        ("ks_reduction_launch_noalloc", N.ReductionConfig(256, 4, 2),
          N.ReductionArgs(None, None, 64, 64, 0, 0, 0, None, 0, None)),
         ("ks_matmul_launch", N.MatmulConfig(128, 256, 64, 4, 2, 16), N.MatmulArgs(None, None, None, 64, 64, 64)),
         ("ks_flash_attention_launch", N.FlashAttentionConfig(256, 128, 2, 1),
