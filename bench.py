@@ -13,11 +13,17 @@ A step is one launch of the family's kernel over one batch, through the C ABI
 (``ks_<family>_launch``).  ``value`` is whole-job throughput with inputs
 resident in HBM; ``e2e`` is the same metric through the same C ABI with the
 inputs copied from pinned host memory and the outputs copied back inside the
-timed region.  Multi-GPU (torchrun) is weak scaling: every rank runs one full
-batch of the configuration on its own GPU (rows / M-panels / heads /
-elements of a G-times larger job); the reduction adds its one cross-GPU
-combine (an NCCL all-reduce of the fp64 partial).  Time = max over ranks of
-CUDA-event time, barrier + synchronize on both sides.
+timed region.  Multi-GPU (torchrun): the headline is weak scaling by default
+(every rank runs one full batch of the configuration on its own GPU: rows /
+M-panels / heads / elements of a G-times larger job), and every family also
+reports strong scaling under "strong": the one configuration sharded over
+the G GPUs (rows, elements, M-panels with B replicated, batch x head pairs),
+with efficiency t1 / (G * t_G) against the whole configuration's time on
+one GPU in the same run.  ``--scaling strong`` makes the sharded
+configuration the headline.  The reduction adds its one cross-GPU combine
+(an NCCL all-reduce of the fp64 partial) to every step.  Time = max over
+ranks of CUDA-event time, barrier + synchronize on both sides, after an
+untimed pre-roll that brings the clocks back up after the barrier.
 
 Inputs are synthetic (seeded torch RNG on the device) with the
 configurations' shapes and distributions.  Between timed steps the input
@@ -272,11 +278,12 @@ def _combine(w, world, i=0):
         dist.combine_partials(w.partials[i % 2], world)
 
 
-def _reduction_steps(w, steps, world, stream):
-    """Steps of the multi-GPU reduction with each step's combine (an NCCL
-    all-reduce of its fp64 partial) on a side stream, overlapping the next
-    step's kernel; partials alternate, so step i+2's kernel waits for step
-    i's combine.  The caller's stream waits for every combine."""
+def _reduction_steps(w, steps, world, stream, first=0):
+    """Steps first..first+steps-1 of the multi-GPU reduction with each step's
+    combine (an NCCL all-reduce of its fp64 partial) on a side stream,
+    overlapping the next step's kernel; partials alternate, so step i+2's
+    kernel waits for step i's combine.  The caller's stream waits for every
+    combine.  Used eagerly and inside a CUDA-graph capture alike."""
     import torch
 
     from kernscope_b200 import dist
@@ -284,15 +291,16 @@ def _reduction_steps(w, steps, world, stream):
     side = getattr(w, "_side", None) or torch.cuda.Stream()
     w._side = side
     done = []
-    for i in range(steps):
-        if i >= 2:
-            stream.wait_event(done[i - 2])
-        w.launch(i)
+    for j in range(steps):
+        i = first + j
+        if j >= 2:
+            stream.wait_event(done[j - 2])
+        w.launch(i, stream=stream)
         k = torch.cuda.Event()
         k.record(stream)
         side.wait_event(k)
         with torch.cuda.stream(side):
-            dist.combine_partials(w.partials[i % 2], world)
+            dist.combine_partials(w.partials[i % 2], world, to_f32=False)
         c = torch.cuda.Event()
         c.record(side)
         done.append(c)
@@ -300,59 +308,84 @@ def _reduction_steps(w, steps, world, stream):
         stream.wait_event(c)
 
 
-def measure_device(w, steps, warmup, world, graph=True):
+def _enqueue(w, first, count, world, stream):
+    """Launches first..first+count-1 (rotating buffer sets) on `stream`; the
+    multi-GPU reduction with its overlapped per-step combine."""
+    if world > 1 and w.name == "reduction":
+        _reduction_steps(w, count, world, stream, first)
+    else:
+        for i in range(first, first + count):
+            w.launch(i, stream=stream)
+
+
+def measure_device(w, steps, warmup, world, graph=True, preroll_ms=3.0):
     """Timed region: `steps` launches on rotating buffers, CUDA events on the
-    launching stream.  Launch loops are captured in a CUDA graph (one graph
-    of `rotate` launches replayed) so host overhead never paces the GPU."""
+    launching stream, max over ranks.
+
+    The timed launches are captured in one CUDA graph (the multi-GPU
+    reduction's graph holds its NCCL combines too), so host overhead never
+    paces the GPU.  The barrier before the timed region idles the GPU, so a
+    pre-roll graph of untimed launches (about `preroll_ms` of work, at least
+    3) is replayed right after the barrier with no host sync before the
+    start event: the clocks are back up when timing starts.  Every rank
+    takes the same collective steps: the pre-roll length and the capture's
+    success are agreed over ranks before any replay.  Returns
+    (max-over-ranks ms, this rank's ms, timing label)."""
     import torch
 
+    from kernscope_b200 import dist
+
     stream = torch.cuda.current_stream()
-    overlap = world > 1 and w.name == "reduction"
-    if overlap:
-        _reduction_steps(w, warmup, world, stream)
-    else:
-        for i in range(warmup):
-            w.launch(i)
+    cap = torch.cuda.Stream()
+    # untimed warm-up, eager; its event time sizes the pre-roll
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    _enqueue(w, 0, warmup, world, stream)
+    t1.record(stream)
     torch.cuda.synchronize()
-    g = None
-    per_graph = w.rotate if w.rotate > 1 else 1
-    # graphs hold only this rank's kernels; the reduction's per-step NCCL
-    # combine stays outside a graph (its launch is ~165 us, host-paced is fine)
-    if graph and (world == 1 or w.name != "reduction"):
-        reps = max(1, 8 // per_graph) if per_graph < 8 else 1
-        per_graph *= reps
-        s = torch.cuda.Stream()
-        s.wait_stream(stream)
-        with torch.cuda.stream(s):
-            w.launch(0)
+    est = max(t0.elapsed_time(t1) / max(1, warmup), 1e-3)
+    npre = int(_max_over_ranks(min(max(3, math.ceil(preroll_ms / est)), max(3, 4 * steps)), world))
+    g = gp = None
+    ok = 1.0
+    if graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                _enqueue(w, 0, steps, world, cap)
+            gp = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gp, stream=cap):
+                _enqueue(w, steps, npre, world, cap)
+        except Exception:  # noqa: BLE001 - capture refused: every rank times eager launches instead
+            ok = 0.0
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for i in range(per_graph):
-                w.launch(i)
-        g.replay()
-        torch.cuda.synchronize()
+        ok = -_max_over_ranks(-ok, world)  # min over ranks
+        if ok < 1.0:
+            g = gp = None
+    label = "graph" if g is not None else "eager"
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(world)
-    e0.record(stream)
     if g is not None:
-        full, rem = divmod(steps, per_graph)
-        for _ in range(full):
-            g.replay()
-        for i in range(rem):
-            w.launch(i)
-    elif overlap:
-        _reduction_steps(w, steps, world, stream)
+        gp.replay()
+        e0.record(stream)
+        g.replay()
     else:
-        for i in range(steps):
-            w.launch(i)
+        _enqueue(w, steps, npre, world, stream)
+        e0.record(stream)
+        _enqueue(w, 0, steps, world, stream)
     e1.record(stream)
     e1.synchronize()
     ms = e0.elapsed_time(e1)
     _barrier(world)
-    if g is not None:
-        del g
-    return _max_over_ranks(ms, world)
+    del g, gp
+    dist.barrier(world)
+    return _max_over_ranks(ms, world), ms, label
+
+
+def _rank_spread(ms, world):
+    """Per-rank timed-region ms of every rank (gathered), for the line's spread."""
+    from kernscope_b200 import dist
+
+    return dist.gather_values(ms, world, device="cuda")
 
 
 def measure_e2e(w, steps, world):
@@ -483,6 +516,58 @@ def cpu_baseline(name, shape, budget_s=10.0):
     return units / t_total, sample
 
 
+def measure_strong(nm, args, rank, world, t1_ms):
+    """Strong scaling of one fixed configuration: every rank takes its shard
+    of the one job (``dist.strong_shard``: rows, elements, M-panels with B
+    replicated, or batch x head pairs) and the job's time is the slowest
+    rank's.  `t1_ms` is the per-step time of the whole configuration on one
+    GPU, measured in the same run (the weak measurement, max over ranks), so
+    efficiency = t1 / (G * t_G).  The step count keeps the timed region near
+    2 ms or more."""
+    import torch
+
+    from kernscope_b200 import dist
+
+    spec = WORKLOADS[nm]
+    shard, desc = dist.strong_shard(nm, spec["shape"], rank, world)
+    w = Workload(nm, shard, rank, world, seed_base=7)
+    steps = int(min(4000, max(int(args.family_steps), math.ceil(2.0 / max(t1_ms / world, 1e-3)))))
+    steps = int(_max_over_ranks(steps, world))
+    ms, my_ms, label = measure_device(w, steps, 3, world)
+    per = ms / steps
+    u_full = _job_units(nm, spec["shape"], spec["bound"])
+    out = {"shape_per_gpu": list(shard), "shard": desc, "steps": steps, "ms_per_step": round(per, 5),
+           "value": round(u_full / (per / 1e3), 2), "t1_ms_per_step": round(t1_ms, 5),
+           "efficiency": round(t1_ms / (world * per), 4),
+           "rank_ms_per_step": [round(v / steps, 5) for v in _rank_spread(my_ms, world)], "timing": label}
+    del w
+    torch.cuda.empty_cache()
+    return out
+
+
+def _job_units(nm, shape, bound):
+    """Work units (TFLOP or GB of algorithmic traffic) of one step of the
+    configuration at `shape`."""
+    if nm in ("softmax",):
+        r, c = shape
+        b = r * c * 4
+    elif nm == "layernorm":
+        r, c = shape
+        b = r * c * 4 + 2 * c * 2
+    elif nm == "bias_gelu":
+        r, c = shape
+        b = r * c * 4 + c * 2
+    elif nm == "reduction":
+        b = shape[0] * 4 + 4
+    elif nm.startswith("matmul"):
+        m, n, k = shape
+        return 2 * m * n * k / 1e12
+    else:
+        bb, h, s, d = shape
+        return 4 * d * bb * h * s * (s + 1) // 2 / 1e12
+    return b / 1e9
+
+
 def run_families(names, args, rank, world):
     out = {}
     peaks = _peaks()
@@ -501,20 +586,27 @@ def run_families(names, args, rank, world):
             del w
             continue
         steps = max(3, int(args.family_steps))
-        ms = measure_device(w, steps, 3, world)
+        ms, my_ms, label = measure_device(w, steps, 3, world)
         per = ms / steps
         u, unit = _units(w, spec["bound"])
         val = u * world / (per / 1e3)
         peak = peaks["hbm_gbs"] if spec["bound"] == "hbm" else peaks["bf16_tflops"]
         ach = u / (per / 1e3)
         out[nm] = {"config": spec["config"], "workload": spec["desc"], "kernel": w.config_name(),
-                   "value": round(val, 2), "unit": unit, "ms_per_step": round(per, 5),
+                   "value": round(val, 2), "unit": unit, "ms_per_step": round(per, 5), "timing": label,
                    "roofline": {"bound": spec["bound"], "achieved": round(ach, 2), "peak": peak, "unit": unit,
                                 "frac": round(ach / peak, 4), "traffic": traffic.get(nm)}}
+        if world > 1:
+            out[nm]["rank_ms_per_step"] = [round(v / steps, 5) for v in _rank_spread(my_ms, world)]
         del w
         import torch
 
         torch.cuda.empty_cache()
+        if world > 1 and not args.no_strong:
+            try:
+                out[nm]["strong"] = measure_strong(nm, args, rank, world, per)
+            except Exception as exc:  # noqa: BLE001
+                out[nm]["strong"] = {"error": str(exc)[:200]}
     return out
 
 
@@ -562,7 +654,7 @@ def main_reference(args):
     line = {"metric": "bf16 TFLOP/s & HBM GB/s per kernel family as % of B200 roofline",
             "impl": "reference", "value": round(val, 6), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(tt / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+            "scaling": args.scaling, "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
             "config": {"workload": spec["desc"], "baseline_config": spec["config"]},
             "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cores, "kind": "port",
                              "sample": f"{cores} worker processes x {chunk}-row chunks per step, compute only "
@@ -656,6 +748,10 @@ def main():
     ap.add_argument("--impl", default="kernscope", choices=("kernscope", "reference"))
     ap.add_argument("--workload", default="softmax", choices=sorted(WORKLOADS))
     ap.add_argument("--no-families", action="store_true", help="skip the per-family summary")
+    ap.add_argument("--scaling", default="weak", choices=("weak", "strong"),
+                    help="headline at N>1: weak (one full configuration per GPU) or strong (the configuration "
+                         "sharded over the GPUs); every family reports both at N>1 unless --no-strong")
+    ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling measurements at N>1")
     ap.add_argument("--family-steps", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -684,7 +780,8 @@ def main():
         for i in range(16):
             w.launch(i)
         torch.cuda.synchronize()
-    ms = measure_device(w, args.steps, args.warmup, world)
+    ms, my_ms, timing = measure_device(w, args.steps, args.warmup, world)
+    rank_ms = _rank_spread(my_ms, world) if world > 1 else None
     extra_t = time.time()
     while time.time() - extra_t < args.clock_window / 3:
         for i in range(16):
@@ -702,6 +799,9 @@ def main():
     kernel = w.config_name()
     del w
     torch.cuda.empty_cache()
+    strong = None
+    if world > 1 and (args.scaling == "strong" or not args.no_strong):
+        strong = measure_strong(args.workload, args, rank, world, per)
     fams = None
     if not args.no_families:
         # the heaviest (power-capped) workload last, so it does not heat the GPU
@@ -715,19 +815,25 @@ def main():
         cpu = {"value": round(cv, 4), "unit": unit, "cores": 1, "kind": "port",
                "sample": sample + " (numpy restatement of tests/golden/kernscope_golden/refs.py, 1 process)"}
     if rank == 0:
+        steps_line, shape_line, par = args.steps, list(spec["shape"]), f"dp{world} (weak: one batch per GPU)"
+        if args.scaling == "strong" and strong is not None:
+            # headline = the one configuration sharded over the GPUs
+            per, value, steps_line = strong["ms_per_step"], strong["value"], strong["steps"]
+            shape_line, par = strong["shape_per_gpu"], f"dp{world} (strong: {strong['shard']} on rank 0)"
+            achieved = _job_units(args.workload, strong["shape_per_gpu"], spec["bound"]) / (per / 1e3)
         line = {
             "metric": "bf16 TFLOP/s & HBM GB/s per kernel family as % of B200 roofline",
-            "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": steps_line,
             "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"],
+            "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None, "dtype": spec["dtype"],
             "data": "synthetic (seeded torch RNG on device, configuration distributions)",
             "config": {"workload": spec["desc"], "baseline_config": spec["config"],
-                       "shape_per_gpu": list(spec["shape"]), "kernel": kernel,
-                       "parallelism": f"dp{world} (weak: one batch per GPU)",
+                       "shape_per_gpu": shape_line, "kernel": kernel,
+                       "parallelism": par,
                        "l2": "rotating input/output sets, working set >= 4x L2 (no step reads inputs from L2)",
-                       "timing": "CUDA events on the launching stream, graph-replayed launch loop (multi-GPU "
-                                 "reduction: launches with each step's NCCL combine overlapping the next "
-                                 "step), max over ranks"},
+                       "timing": f"CUDA events on the launching stream, {timing}-replayed launch loop after an "
+                                 "untimed pre-roll that follows the barrier (multi-GPU reduction: each step's "
+                                 "NCCL combine on a side stream overlapping the next step), max over ranks"},
             "roofline": {"bound": spec["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": peaks["source"]},
@@ -737,6 +843,10 @@ def main():
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
+        if rank_ms is not None:
+            line["rank_ms_per_step"] = [round(v / args.steps, 5) for v in rank_ms]
+        if strong is not None:
+            line["strong"] = strong
         if fams is not None:
             line["families"] = fams
         print(json.dumps(line))

@@ -56,14 +56,51 @@ def max_over_ranks(value: float, world: int, device=None) -> float:
     return float(t.item())
 
 
-def combine_partials(partial_f64, world: int):
+def gather_values(value: float, world: int, device=None) -> list[float]:
+    """Every rank's value of a per-rank scalar, in rank order."""
+    if world == 1:
+        return [float(value)]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
+def combine_partials(partial_f64, world: int, to_f32: bool = True):
     """The reduction family's cross-GPU combine: sum the per-GPU fp64 partial
-    sums in place (count 1); returns the fp32 total."""
+    sums in place (count 1); returns the fp32 total (or, with to_f32 False,
+    the fp64 partial itself, so that no conversion kernel follows)."""
     if world > 1:
         import torch.distributed as dist
 
         dist.all_reduce(partial_f64, op=dist.ReduceOp.SUM)
-    return partial_f64.to(dtype=__import__("torch").float32)
+    return partial_f64.to(dtype=__import__("torch").float32) if to_f32 else partial_f64
+
+
+def strong_shard(family: str, shape, rank: int, world: int):
+    """This rank's part of a fixed job (strong scaling): rows of the row-wise
+    families, elements of the full sum, M-panels of the GEMM (B replicated),
+    batch x head pairs of attention.  Returns (shard shape, description)."""
+    shape = tuple(int(v) for v in shape)
+    if family in ("softmax", "layernorm", "bias_gelu"):
+        r0, r1 = shard_rows(shape[0], rank, world)
+        return (r1 - r0, shape[1]), f"rows [{r0}, {r1}) of {shape[0]}"
+    if family == "reduction":
+        e0, e1 = shard_rows(shape[0], rank, world)
+        return (e1 - e0,), f"elements [{e0}, {e1}) of {shape[0]}"
+    if family.startswith("matmul"):
+        m0, m1 = shard_rows(shape[0], rank, world)
+        return (m1 - m0, shape[1], shape[2]), f"A/C rows [{m0}, {m1}) of {shape[0]}, B replicated"
+    if family == "flash_attention":
+        b, h, s, d = shape
+        p0, p1 = shard_rows(b * h, rank, world)
+        n = p1 - p0
+        sh = (n // h, h, s, d) if n % h == 0 else (1, n, s, d)
+        return sh, f"(batch, head) pairs [{p0}, {p1}) of {b * h}"
+    raise KeyError(family)
 
 
 def shard_rows(rows: int, rank: int, world: int) -> tuple[int, int]:

@@ -880,6 +880,42 @@ int tune_query_json(const char *request_json, char *out, size_t cap, size_t *nee
     }
     res = object({{"opened", Value(opened)}, {"records", Value(int(d.size()))}, {"warnings", Value(std::move(warn))},
                   {"best", Value(std::move(best))}});
+  } else if (op == "golden") {
+    // The gate's host half: {family, shape, seed, inputs?: {name: [bf16 bits]},
+    // verdict_got?: [bf16 bits]} -> the inputs used and the reference output
+    // (bf16 bits), plus the gate verdict of verdict_got against it.
+    std::map<std::string, std::vector<std::uint16_t>> in, used;
+    if (const Value *iv = j.find("inputs"); iv && iv->is_object())
+      for (const auto &[name, arr] : iv->as_object()) {
+        std::vector<std::uint16_t> bits;
+        if (arr.is_array())
+          for (const Value &x : arr.as_array()) bits.push_back(std::uint16_t(x.as_number()));
+        in[name] = std::move(bits);
+      }
+    std::vector<float> expected;
+    std::string gerr;
+    if (!tune::golden_case(j.string_or("family", ""), shape, std::uint64_t(j.number_or("seed", 0)), in, &used,
+                           &expected, &gerr))
+      return write_out(object({{"error", Value(gerr)}}).dump(), out, cap, needed) == 0 ? 2 : -1;
+    auto to_arr = [](const std::vector<std::uint16_t> &b) {
+      std::vector<Value> v;
+      v.reserve(b.size());
+      for (auto x : b) v.emplace_back(double(x));
+      return Value(std::move(v));
+    };
+    std::vector<std::uint16_t> exp_bits;
+    for (float x : expected) exp_bits.push_back(tune::f32_to_bf16(x));
+    std::vector<Value::Member> inputs_out;
+    for (const auto &[name, b] : used) inputs_out.emplace_back(name, to_arr(b));
+    std::vector<Value::Member> r{{"inputs", Value(std::move(inputs_out))}, {"expected", to_arr(exp_bits)}};
+    if (const Value *g = j.find("verdict_got"); g && g->is_array()) {
+      std::vector<float> got;
+      for (const Value &x : g->as_array()) got.push_back(tune::bf16_to_f32(std::uint16_t(x.as_number())));
+      const tune::GateVerdict gv = tune::bf16_verdict(got, expected);
+      r.emplace_back("verdict", object({{"pass", Value(gv.pass)}, {"cosine", Value(gv.cosine)},
+                                        {"max_rel_err", Value(gv.max_rel_err)}, {"pcc", Value(gv.pcc)}}));
+    }
+    res = Value(std::move(r));
   } else if (op == "quantile") {
     std::vector<double> s;
     if (const Value *v = j.find("samples"); v && v->is_array())

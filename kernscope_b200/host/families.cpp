@@ -8,6 +8,7 @@
 #include <map>
 #include <sstream>
 
+#include "golden.h"
 #include "hwmodel.h"
 
 namespace kernscope::tune {
@@ -15,35 +16,10 @@ namespace kernscope::tune {
 // ---------------------------------------------------------------------------
 // bf16, seeded inputs, device buffers
 // ---------------------------------------------------------------------------
-std::uint16_t f32_to_bf16(float f) {
-  std::uint32_t u;
-  std::memcpy(&u, &f, 4);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return std::uint16_t((u >> 16) | 0x40u);  // NaN stays NaN
-  const std::uint32_t rounding = 0x7fffu + ((u >> 16) & 1u);                    // round to nearest even
-  return std::uint16_t((u + rounding) >> 16);
-}
-float bf16_to_f32(std::uint16_t h) {
-  const std::uint32_t u = std::uint32_t(h) << 16;
-  float f;
-  std::memcpy(&f, &u, 4);
-  return f;
-}
-static float rbf(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+std::uint16_t f32_to_bf16(float f) { return golden::to_bf16_bits(f); }
+float bf16_to_f32(std::uint16_t h) { return golden::from_bf16_bits(h); }
 
 namespace {
-
-// splitmix64 stream -> uniform doubles in [lo, hi)
-struct Rng {
-  std::uint64_t s;
-  explicit Rng(std::uint64_t seed) : s(seed * 0x9E3779B97F4A7C15ull + 0x632BE59BD9B4E019ull) {}
-  std::uint64_t next() {
-    std::uint64_t z = (s += 0x9E3779B97F4A7C15ull);
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-  }
-  double uniform(double lo, double hi) { return lo + (hi - lo) * double(next() >> 11) * 0x1.0p-53; }
-};
 
 // bf16 tensor with host copy (bf16 bits + fp32 view) and a device copy
 struct DevBuf {
@@ -61,18 +37,23 @@ struct DevBuf {
   }
 };
 
+// The next n draws of the reference profile's uniform(lo, hi), rounded to
+// bf16 (inputs.py:73-106 through golden::draw_bf16), with an fp32 view.
 struct HostBf16 {
   std::vector<std::uint16_t> bits;
   std::vector<float> f;
-  void fill_uniform(Rng &r, size_t n, double lo, double hi) {
-    bits.resize(n);
-    f.resize(n);
-    for (size_t i = 0; i < n; ++i) {
-      bits[i] = f32_to_bf16(float(r.uniform(lo, hi)));
-      f[i] = bf16_to_f32(bits[i]);
-    }
+  void fill_uniform(golden::Generator &g, size_t n, double lo, double hi) {
+    set_bits(golden::draw_bf16(g, n, lo, hi));
+  }
+  void set_bits(std::vector<std::uint16_t> b) {
+    bits = std::move(b);
+    f.resize(bits.size());
+    for (size_t i = 0; i < bits.size(); ++i) f[i] = bf16_to_f32(bits[i]);
   }
 };
+
+// A session's host inputs by the reference's names (inputs.py keys).
+using NamedInputs = std::vector<std::pair<const char *, HostBf16 *>>;
 
 int upload(DevBuf &d, const void *src, size_t bytes) {
   int s = d.alloc(bytes);
@@ -166,29 +147,15 @@ std::string canonical_config(const json &cfg) {
 // ---------------------------------------------------------------------------
 GateVerdict bf16_verdict(const std::vector<float> &a, const std::vector<float> &r) {
   GateVerdict v;
+  const golden::Verdict rv = golden::verdict(a, r);
+  v.cosine = rv.cosine;
+  v.max_rel_err = rv.max_rel_err;
+  v.pcc = rv.pcc;
+  // diagnostics: per-element error with a 2^-8 rms floor, norm-wise error
   const size_t n = std::min(a.size(), r.size());
-  double dot = 0, na = 0, nr = 0, ma = 0, mr = 0, mre = 0, ss = 0, se = 0;
-  for (size_t i = 0; i < n; ++i) {
-    dot += double(a[i]) * r[i];
-    na += double(a[i]) * a[i];
-    nr += double(r[i]) * r[i];
-    ma += a[i];
-    mr += r[i];
-    mre = std::max(mre, std::fabs(double(a[i]) - r[i]) / (std::fabs(double(r[i])) + 1e-6));
-  }
-  v.cosine = (na > 0 && nr > 0) ? dot / std::sqrt(na * nr) : (na == 0 && nr == 0 ? 1.0 : 0.0);
-  v.max_rel_err = mre;
-  ma /= double(std::max<size_t>(n, 1));
-  mr /= double(std::max<size_t>(n, 1));
-  double sxy = 0, sxx = 0, syy = 0;
-  for (size_t i = 0; i < n; ++i) {
-    sxy += (a[i] - ma) * (r[i] - mr);
-    sxx += (a[i] - ma) * (a[i] - ma);
-    syy += (r[i] - mr) * (r[i] - mr);
-  }
-  v.pcc = (sxx > 0 && syy > 0) ? sxy / std::sqrt(sxx * syy) : 1.0;
+  double nr = 0, ss = 0, se = 0, fmax = 0;
+  for (size_t i = 0; i < n; ++i) nr += double(r[i]) * r[i];
   const double rms = std::sqrt(nr / double(std::max<size_t>(n, 1)));
-  double fmax = 0;
   for (size_t i = 0; i < n; ++i) {
     const double den = std::max(std::fabs(double(r[i])), rms * std::ldexp(1.0, -8));
     const double e = std::fabs(double(a[i]) - r[i]);
@@ -198,8 +165,8 @@ GateVerdict bf16_verdict(const std::vector<float> &a, const std::vector<float> &
   }
   v.floor_rel_err = fmax;
   v.norm_rel_err = ss > 0 ? std::sqrt(se / ss) : std::sqrt(se);
-  v.pass = v.cosine >= 0.999 && v.pcc >= 0.99 && v.floor_rel_err <= 1e-2 && v.norm_rel_err <= 1e-2;
-  v.criterion = "cosine>=0.999, pcc>=0.99, floor rel-err<=1e-2, norm rel-err<=1e-2";
+  v.pass = rv.pass;
+  v.criterion = "reference verdict: cosine>=0.999, max_rel_err(eps 1e-6)<=1e-2, pcc>=0.99";
   return v;
 }
 
@@ -232,9 +199,14 @@ class MatmulSession : public Session {
   DevBuf da, db, dc;
   int init(std::int64_t M, std::int64_t N, std::int64_t K, std::uint64_t seed) {
     m = M, n = N, k = K;
-    Rng r(seed);
+    golden::Generator r(seed);  // inputs.py:77-80: a, then b
     a.fill_uniform(r, size_t(m * k), -1, 1);
     b.fill_uniform(r, size_t(k * n), -1, 1);
+    return host_only ? KS_OK : upload_all();
+  }
+  bool host_only = false;  // inputs and reference only (no device buffers)
+  NamedInputs named() { return {{"a", &a}, {"b", &b}}; }
+  int upload_all() {
     int s = upload(da, a.bits.data(), a.bits.size() * 2);
     if (s == KS_OK) s = upload(db, b.bits.data(), b.bits.size() * 2);
     if (s == KS_OK) s = dc.alloc(size_t(m * n) * 2);
@@ -246,18 +218,9 @@ class MatmulSession : public Session {
     return ks_matmul_launch(&c, &args, st);
   }
   int output(std::vector<float> *o) override { return download_bf16(dc, size_t(m * n), o); }
-  void reference(std::vector<float> *o) const override {
+  void reference(std::vector<float> *o) const override {  // refs.py:54-56
     o->assign(size_t(m * n), 0.f);
-    std::vector<float> acc(static_cast<size_t>(n));
-    for (std::int64_t i = 0; i < m; ++i) {
-      std::fill(acc.begin(), acc.end(), 0.f);
-      for (std::int64_t kk = 0; kk < k; ++kk) {
-        const float av = a.f[size_t(i * k + kk)];
-        const float *brow = &b.f[size_t(kk * n)];
-        for (std::int64_t j = 0; j < n; ++j) acc[size_t(j)] += av * brow[j];
-      }
-      for (std::int64_t j = 0; j < n; ++j) (*o)[size_t(i * n + j)] = rbf(acc[size_t(j)]);
-    }
+    golden::matmul(a.f.data(), b.f.data(), m, n, k, o->data());
   }
   int corrupt_output(void *st) override { return ks_gpu_memset(dc.p, 0, size_t(m * n) * 2, st); }
 };
@@ -365,65 +328,53 @@ class FlashSession : public Session {
   int init(const FaShape &s, bool c, std::uint64_t seed) {
     sh = s;
     causal = c;
-    Rng r(seed);
-    const double sc = 1.0 / std::sqrt(double(s.d));  // the reference profile (inputs.py:98-105)
+    golden::Generator r(seed);
+    // the reference profile (inputs.py:98-105): q, k ~ U(-1/sqrt d, 1/sqrt d),
+    // v ~ U(-1, 1), each drawn for every head at once (one head = the
+    // reference's single-head draws exactly)
+    const double sc = 1.0 / std::sqrt(double(s.d));
     q.fill_uniform(r, size_t(s.bh * s.nq * s.d), -sc, sc);
     k.fill_uniform(r, size_t(s.bh * s.nk * s.d), -sc, sc);
     v.fill_uniform(r, size_t(s.bh * s.nk * s.d), -1, 1);
+    return host_only ? KS_OK : upload_all();
+  }
+  bool host_only = false;  // inputs and reference only (no device buffers)
+  NamedInputs named() { return {{"q", &q}, {"k", &k}, {"v", &v}}; }
+  int upload_all() {
     int st = upload(dq, q.bits.data(), q.bits.size() * 2);
     if (st == KS_OK) st = upload(dk, k.bits.data(), k.bits.size() * 2);
     if (st == KS_OK) st = upload(dv, v.bits.data(), v.bits.size() * 2);
     if (st == KS_OK) st = dout.alloc(q.bits.size() * 2);
     return st;
   }
+  bool tensor_path = false;  // the last launched config ran on the tcgen05 kernels
   int launch(const json &cfg, void *st) override {
     ks_flash_attention_config c{iget(cfg, "tile_m", 256), iget(cfg, "tile_n", 128), iget(cfg, "stages", 2),
                                 causal ? 1 : 0};
+    tensor_path = sh.d == 128 || (sh.d == 64 && c.tile_m == 256);
     ks_flash_attention_args a{dq.p, dk.p, dv.p, dout.p, 1, sh.bh, sh.nq, sh.nk, sh.d, 0.f};
     return ks_flash_attention_launch(&c, &a, st);
   }
   int output(std::vector<float> *o) override { return download_bf16(dout, size_t(sh.bh * sh.nq * sh.d), o); }
-  void reference(std::vector<float> *o) const override {
+  void reference(std::vector<float> *o) const override {  // refs.py:113-142 per head
     o->assign(size_t(sh.bh * sh.nq * sh.d), 0.f);
-    const float scale = 1.f / std::sqrt(float(sh.d));
-    std::vector<float> srow(static_cast<size_t>(sh.nk)), acc(static_cast<size_t>(sh.d));
     for (std::int64_t h = 0; h < sh.bh; ++h)
-      for (std::int64_t i = 0; i < sh.nq; ++i) {
-        const float *qi = &q.f[size_t((h * sh.nq + i) * sh.d)];
-        float mx = -INFINITY;
-        for (std::int64_t j = 0; j < sh.nk; ++j) {
-          if (causal && j > i) {
-            srow[size_t(j)] = -INFINITY;
-            continue;
-          }
-          const float *kj = &k.f[size_t((h * sh.nk + j) * sh.d)];
-          float s = 0.f;
-          for (std::int64_t c = 0; c < sh.d; ++c) s += qi[c] * kj[c];
-          srow[size_t(j)] = s * scale;
-          mx = std::max(mx, srow[size_t(j)]);
-        }
-        float sum = 0.f;
-        for (std::int64_t j = 0; j < sh.nk; ++j) {
-          srow[size_t(j)] = std::exp(srow[size_t(j)] - mx);
-          sum += srow[size_t(j)];
-        }
-        std::fill(acc.begin(), acc.end(), 0.f);
-        for (std::int64_t j = 0; j < sh.nk; ++j) {
-          const float p = srow[size_t(j)] / sum;
-          if (p == 0.f) continue;
-          const float *vj = &v.f[size_t((h * sh.nk + j) * sh.d)];
-          for (std::int64_t c = 0; c < sh.d; ++c) acc[size_t(c)] += p * vj[c];
-        }
-        for (std::int64_t c = 0; c < sh.d; ++c) (*o)[size_t((h * sh.nq + i) * sh.d + c)] = rbf(acc[size_t(c)]);
-      }
+      golden::attention(&q.f[size_t(h * sh.nq * sh.d)], &k.f[size_t(h * sh.nk * sh.d)],
+                        &v.f[size_t(h * sh.nk * sh.d)], sh.nq, sh.nk, sh.d, causal,
+                        o->data() + h * sh.nq * sh.d);
   }
-  // The tensor-core path rounds P to bf16 before P V (2^-9 per probability):
-  // per element |a - r| <= 1e-2 * rho, rho = softmax |V| (row weights of |V|).
+  // The CUDA-core kernel (fp32 throughout) is judged by the reference verdict
+  // as it stands.  The tensor-core path rounds P to bf16 before P V (2^-9 per
+  // probability), which no tensor-core attention avoids; on outputs near zero
+  // that alone exceeds max_rel_err's 1e-2 with eps 1e-6, so for that path the
+  // per-element term becomes |a - r| <= 1e-2 * rho, rho = softmax |V| (the
+  // scale of the P rounding error), beside the reference's cosine and pcc
+  // and a norm-wise error <= 1e-2.
   GateVerdict verdict(const std::vector<float> &got, const std::vector<float> &ref) const override {
     GateVerdict gv = bf16_verdict(got, ref);
-    if (sh.d != 128 && sh.d != 64) return gv;  // only d = 64 and 128 can take the tensor-core path
+    if (!tensor_path) return gv;
     double worst = 0.0;
-    const float scale = 1.f / std::sqrt(float(sh.d));
+    const float sd = float(std::sqrt(double(sh.d)));
     std::vector<float> srow(static_cast<size_t>(sh.nk));
     for (std::int64_t h = 0; h < sh.bh; ++h)
       for (std::int64_t i = 0; i < sh.nq; ++i) {
@@ -435,7 +386,7 @@ class FlashSession : public Session {
             const float *kj = &k.f[size_t((h * sh.nk + j) * sh.d)];
             s = 0.f;
             for (std::int64_t c = 0; c < sh.d; ++c) s += qi[c] * kj[c];
-            s *= scale;
+            s /= sd;
           }
           srow[size_t(j)] = s;
           mx = std::max(mx, s);
@@ -577,9 +528,9 @@ class RowSession : public Session {
     cols = c;
     gelu = g;
     axis = ax;
-    Rng rng(seed);
-    int st = KS_OK;
+    golden::Generator rng(seed);
     const size_t n = size_t(r * c);
+    out_n = k == RowKind::kReduction ? (axis == -1 ? 1 : size_t(c)) : n;
     // distributions of the reference profile (inputs.py:77-97)
     switch (k) {
       case RowKind::kSoftmax: x.fill_uniform(rng, n, -2, 2); break;
@@ -601,14 +552,26 @@ class RowSession : public Session {
         }
         break;
     }
-    if (k == RowKind::kReduction && axis == -1)
+    return host_only ? KS_OK : upload_all();
+  }
+  bool host_only = false;  // inputs and reference only (no device buffers)
+  NamedInputs named() {
+    switch (kind) {
+      case RowKind::kLayerNorm: return {{"x", &x}, {"gamma", &p1}, {"beta", &p2}};
+      case RowKind::kBiasGelu: return {{"x", &x}, {"bias", &p1}};
+      default: return {{"x", &x}};
+    }
+  }
+  int upload_all() {
+    const size_t n = size_t(rows * cols);
+    int st = KS_OK;
+    if (kind == RowKind::kReduction && axis == -1)
       st = upload(dx, xf32.data(), n * 4);
     else
       st = upload(dx, x.bits.data(), n * 2);
     if (st == KS_OK && !p1.bits.empty()) st = upload(dp1, p1.bits.data(), p1.bits.size() * 2);
     if (st == KS_OK && !p2.bits.empty()) st = upload(dp2, p2.bits.data(), p2.bits.size() * 2);
-    out_n = k == RowKind::kReduction ? (axis == -1 ? 1 : size_t(c)) : n;
-    const size_t out_bytes = k == RowKind::kReduction && axis == -1 ? 4 : out_n * 2;
+    const size_t out_bytes = kind == RowKind::kReduction && axis == -1 ? 4 : out_n * 2;
     if (st == KS_OK) st = dout.alloc(out_bytes);
     return st;
   }
@@ -663,58 +626,22 @@ class RowSession : public Session {
   }
 
   void reference(std::vector<float> *o) const override {
-    const std::int64_t R = rows, C = cols;
     o->assign(out_n, 0.f);
     switch (kind) {
-      case RowKind::kSoftmax:  // refs.py:79-84
-        for (std::int64_t r = 0; r < R; ++r) {
-          const float *xr = &x.f[size_t(r * C)];
-          float mx = -INFINITY;
-          for (std::int64_t c = 0; c < C; ++c) mx = std::max(mx, xr[c]);
-          std::vector<float> e(static_cast<size_t>(C));
-          float s = 0.f;
-          for (std::int64_t c = 0; c < C; ++c) s += (e[size_t(c)] = std::exp(xr[c] - mx));
-          for (std::int64_t c = 0; c < C; ++c) (*o)[size_t(r * C + c)] = rbf(e[size_t(c)] / s);
-        }
+      case RowKind::kSoftmax: golden::softmax(x.f.data(), rows, cols, o->data()); break;  // refs.py:79-84
+      case RowKind::kLayerNorm:  // refs.py:87-99
+        golden::layernorm(x.f.data(), p1.f.data(), p2.f.data(), rows, cols, 1e-5f, o->data());
         break;
-      case RowKind::kLayerNorm:  // refs.py:87-99, two-pass biased variance
-        for (std::int64_t r = 0; r < R; ++r) {
-          const float *xr = &x.f[size_t(r * C)];
-          double s = 0;
-          for (std::int64_t c = 0; c < C; ++c) s += xr[c];
-          const float mean = float(s / double(C));
-          double q = 0;
-          for (std::int64_t c = 0; c < C; ++c) q += double(xr[c] - mean) * double(xr[c] - mean);
-          const float var = float(q / double(C));
-          const float inv = 1.f / std::sqrt(var + 1e-5f);
-          for (std::int64_t c = 0; c < C; ++c)
-            (*o)[size_t(r * C + c)] = rbf((xr[c] - mean) * inv * p1.f[size_t(c)] + p2.f[size_t(c)]);
-        }
-        break;
-      case RowKind::kBiasGelu:  // refs.py:59-76 (erf in double, like math.erf)
-        for (std::int64_t i = 0; i < R * C; ++i) {
-          const float t = rbf(x.f[size_t(i)] + p1.f[size_t(i % C)]);
-          float y;
-          if (gelu == KS_GELU_TANH) {
-            const double u = std::sqrt(2.0 / M_PI) * (t + 0.044715 * double(t) * t * t);
-            y = float(0.5 * t * (1.0 + std::tanh(u)));
-          } else {
-            const float e = float(std::erf(double(t) * (1.0 / std::sqrt(2.0))));
-            y = 0.5f * t * (1.f + e);
-          }
-          (*o)[size_t(i)] = rbf(y);
-        }
+      case RowKind::kBiasGelu:  // refs.py:59-76 (erf), or the tanh extension
+        golden::bias_gelu(x.f.data(), p1.f.data(), rows, cols, gelu == KS_GELU_TANH, o->data());
         break;
       case RowKind::kReduction:
-        if (axis == -1) {
+        if (axis == -1) {  // the full fp32 sum extension, judged against an fp64 sum
           double s = 0;
           for (float v : xf32) s += v;
           (*o)[0] = float(s);
         } else {  // refs.py:102-110
-          std::vector<float> acc(static_cast<size_t>(C), 0.f);
-          for (std::int64_t r = 0; r < R; ++r)
-            for (std::int64_t c = 0; c < C; ++c) acc[size_t(c)] += x.f[size_t(r * C + c)];
-          for (std::int64_t c = 0; c < C; ++c) (*o)[size_t(c)] = rbf(acc[size_t(c)]);
+          golden::reduction_axis0(x.f.data(), rows, cols, o->data());
         }
         break;
     }
@@ -1098,6 +1025,57 @@ const Family *find_family(const std::string &name) {
   if (name == "bias_gelu:tanh") return &r.bias_gelu_tanh;
   if (name == "reduction") return &r.reduction;
   return nullptr;
+}
+
+bool golden_case(const std::string &family, const std::vector<std::int64_t> &shape, std::uint64_t seed,
+                 const std::map<std::string, std::vector<std::uint16_t>> &inputs,
+                 std::map<std::string, std::vector<std::uint16_t>> *used, std::vector<float> *expected,
+                 std::string *error) {
+  const Family *f = find_family(family);
+  if (!f || !f->check_shape(shape, error)) {
+    if (error && !f) *error = "unknown family '" + family + "'";
+    return false;
+  }
+  // the session classes with host_only set: generation and reference only
+  std::unique_ptr<Session> keep;
+  NamedInputs named;
+  if (f == find_family("matmul")) {
+    auto p = std::make_unique<MatmulSession>();
+    p->host_only = true;
+    p->init(shape[0], shape[1], shape[2], seed);
+    named = p->named();
+    keep = std::move(p);
+  } else if (f == find_family("flash_attention") || f == find_family("flash_attention:causal")) {
+    auto p = std::make_unique<FlashSession>();
+    p->host_only = true;
+    p->init(fa_shape(shape), f == find_family("flash_attention:causal"), seed);
+    named = p->named();
+    keep = std::move(p);
+  } else {
+    const auto *rf = static_cast<const RowFamily *>(f);
+    if (rf->kind == RowKind::kReduction && shape.size() == 1) {
+      if (error) *error = "the full fp32 sum has no bf16 golden case";
+      return false;
+    }
+    auto p = std::make_unique<RowSession>();
+    p->host_only = true;
+    p->init(rf->kind, shape[0], shape[1], rf->gelu, 0, seed);
+    named = p->named();
+    keep = std::move(p);
+  }
+  for (auto &[name, buf] : named) {
+    if (auto it = inputs.find(name); it != inputs.end()) {
+      if (it->second.size() != buf->bits.size()) {
+        if (error) *error = std::string("input '") + name + "' has " + std::to_string(it->second.size()) +
+                            " elements, the shape needs " + std::to_string(buf->bits.size());
+        return false;
+      }
+      buf->set_bits(it->second);
+    }
+    if (used) (*used)[name] = buf->bits;
+  }
+  keep->reference(expected);
+  return true;
 }
 
 const std::vector<std::string> &family_names() {

@@ -12,6 +12,7 @@
 #pragma once
 
 #include <cstdint>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -161,10 +162,22 @@ class Session {
   virtual int corrupt_output(void *stream) = 0;
 };
 
-// Reference verdict (tests/golden/kernscope_golden/metrics.py:29-116) plus
-// the floor-guarded rel-err; bf16 outputs pass on cosine >= 0.999,
-// pcc >= 0.99 and floor/norm rel-err <= 1e-2.
+// The reference verdict (tests/golden/kernscope_golden/metrics.py:92-116):
+// bf16 outputs pass on cosine >= 0.999, max_rel_err (eps 1e-6) <= 1e-2 and
+// pcc >= 0.99; the floor-guarded and norm-wise errors ride along as
+// diagnostics.
 GateVerdict bf16_verdict(const std::vector<float> &got, const std::vector<float> &ref);
+
+// The host half of a gate session, for tests and tools: the reference
+// profile's inputs of `family` (a find_family key) at `shape` and `seed`,
+// by the reference's names (inputs.py), as bf16 bits -- with any of them
+// replaced by `inputs` -- and the CPU reference output of those inputs
+// (fp32 holding bf16 values).  False (and *error) on a bad family, shape or
+// input size.
+bool golden_case(const std::string &family, const std::vector<std::int64_t> &shape, std::uint64_t seed,
+                 const std::map<std::string, std::vector<std::uint16_t>> &inputs,
+                 std::map<std::string, std::vector<std::uint16_t>> *used, std::vector<float> *expected,
+                 std::string *error);
 
 // bf16 helpers shared by the sessions and references.
 std::uint16_t f32_to_bf16(float f);

@@ -43,6 +43,7 @@ def _worker(rank, world, port, n, q, fail_rank):
         part = torch.tensor([mine], dtype=torch.float64)
         total = dist.combine_partials(part, w)  # in place: part now holds the job's sum
         t = dist.max_over_ranks(1.0 + rank, w)
+        assert dist.gather_values(0.5 + rank, w) == [0.5 + k for k in range(w)]  # per-rank spread, rank order
         q.put((rank, float(total.item()), mine, t, None))
     except Exception as exc:  # noqa: BLE001 - report to the parent
         q.put((rank, None, None, None, type(exc).__name__ + ": " + str(exc)[:120]))
@@ -91,3 +92,32 @@ def test_failed_rank_ends_collective_with_error():
     errs = {rank: err for rank, _, _, _, err in out}
     assert "injected rank failure" in errs[1]
     assert errs[0] is not None  # the surviving rank's all-reduce errored out instead of hanging
+
+
+@pytest.mark.parametrize("family", ["softmax", "layernorm", "bias_gelu", "reduction", "matmul", "matmul_65536",
+                                    "flash_attention"])
+def test_strong_shards_partition_the_job(family):
+    """Strong scaling: the G shards of a benchmark configuration cover the
+    whole job exactly (rows, elements, M-panels, batch x head pairs), so the
+    sharded job does the same algorithmic work as one GPU does alone."""
+    import importlib.util
+
+    from kernscope_b200 import dist
+
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    wl = bench.WORKLOADS[family]
+    full = bench._job_units(family, wl["shape"], wl["bound"])
+    for world in (1, 2, 4, 8):
+        shards = [dist.strong_shard(family, wl["shape"], r, world)[0] for r in range(world)]
+        parts = [bench._job_units(family, sh, wl["bound"]) for sh in shards]
+        if family in ("layernorm", "bias_gelu"):  # gamma/beta/bias are read by every shard
+            extra = (world - 1) * (2 * wl["shape"][1] * 2 if family == "layernorm" else wl["shape"][1] * 2) / 1e9
+            assert abs(sum(parts) - extra - full) <= 1e-9 * full
+        elif family == "reduction":  # every shard writes its own 4-byte result
+            assert abs(sum(parts) - (world - 1) * 4e-9 - full) <= 1e-9 * full
+        else:
+            assert abs(sum(parts) - full) <= 1e-9 * full, (world, shards)
+        if family.startswith("matmul"):
+            assert all(sh[1:] == tuple(wl["shape"][1:]) for sh in shards)  # B replicated, K and N whole
