@@ -4,7 +4,8 @@
 // tiles in shared memory and accumulates with scalar FMAs.  Here:
 //
 //   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256),
-//     raster grouped by `group_m` M-tiles for L2 reuse;
+//     raster grouped by `group_m` M-tiles for L2 reuse, or (group_m 0)
+//     planned from the L2 size: M-groups or B-resident N-bands;
 //   * warp 0 (one lane) is the TMA producer: per K-block of 64 it loads the
 //     A box [128 rows x 64 K] and BN/64 B boxes [64 K x 64 N], all with the
 //     128-byte swizzle, into a STAGES-deep shared-memory ring (full/empty
@@ -51,7 +52,24 @@ struct MmLayout {
                                         : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
 };
 
-KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &tn) {
+// Tile t (of num_m x num_n) in raster order.  raster > 0: groups of
+// `raster` M-tiles, M fastest within a group, so each group streams all of B
+// once.  raster < 0: bands of -raster N-tiles, N fastest within a band, so a
+// band's B panels stay in L2 while every M-tile passes and A is streamed once
+// per band (the cheaper order when A is much larger than B).
+KS_DEV void tile_coords(int t, int num_m, int num_n, int raster, int &tm, int &tn) {
+  if (raster < 0) {
+    const int band = -raster;
+    const int per_band = band * num_m;
+    const int b = t / per_band;
+    const int first_n = b * band;
+    const int bn = min(num_n - first_n, band);
+    const int r = t - b * per_band;
+    tm = r / bn;
+    tn = first_n + r % bn;
+    return;
+  }
+  const int group_m = raster;
   const int group_size = group_m * num_n;
   const int g = t / group_size;
   const int first_m = g * group_m;
@@ -64,7 +82,7 @@ KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     uint16_t *__restrict__ c, int M, int N, int K, int group_m, int b3d, KsWait wait) {
+                     uint16_t *__restrict__ c, int M, int N, int K, int raster, int b3d, KsWait wait) {
   using L = MmLayout<BN, STAGES, ACC>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
@@ -115,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      tile_coords(t, num_m, num_n, raster, tm, tn);
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait(empty + stage, phase ^ 1u, abort, wait)) {
           ok = false;
@@ -196,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ks_mbar_wait(tfull + acc, acc_phase, abort, wait)) break;
       ks_tc_fence_after();
       int tm, tn;
-      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      tile_coords(t, num_m, num_n, raster, tm, tn);
       const int64_t row = int64_t(tm) * kBM + row_in_tile;
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -273,7 +291,7 @@ struct Mm2Layout {
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                      uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
+                      uint16_t *__restrict__ c, int M, int N, int K, int raster, KsWait wait) {
   using L = Mm2Layout<BN, STAGES, ACC>;
   constexpr int kPM = 2 * kBM;  // rows per pair tile
   extern __shared__ uint8_t smem_raw[];
@@ -328,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int t = pair; t < num_tiles && ok; t += num_pairs) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      tile_coords(t, num_m, num_n, raster, tm, tn);
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait_cluster(empty + stage, phase ^ 1u, abort, wait)) {
           ok = false;
@@ -418,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ks_mbar_wait_cluster(tfull + acc, acc_phase, abort, wait)) break;
       ks_tc_fence_after();
       int tm, tn;
-      tile_coords(t, num_m, num_n, group_m, tm, tn);
+      tile_coords(t, num_m, num_n, raster, tm, tn);
       const int64_t row = int64_t(tm) * kPM + row_in_tile;
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -504,6 +522,42 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(const uint16_t *__rest
     }
 }
 
+// The tile raster of a launch.  group_m > 0 is the configured M-group.
+// group_m == 0 plans from the L2: the in-flight tiles (one per CTA, or per
+// CTA pair) plus the panels kept for reuse must fit in ~70 % of the L2.
+//   * M-groups of mb tiles: A read once, B once per group;
+//   * N-bands of nb tiles: B read once, A once per band;
+// each with the widest group that fits, and the order with less modelled
+// DRAM traffic wins (65536 x 8192 x 8192: N-bands of 17 tiles, 2.1 GB of
+// reads, against 32 B streams with M-groups of 16).
+int plan_raster(int group_m, int64_t M, int64_t N, int64_t K, int tile_m, int tile_n, int64_t inflight) {
+  if (group_m > 0) return group_m;
+  int dev = 0, l2 = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) != cudaSuccess ||
+      l2 <= 0)
+    l2 = 126 << 20;
+  const double budget = 0.7 * double(l2);
+  const int64_t num_m = (M + tile_m - 1) / tile_m, num_n = (N + tile_n - 1) / tile_n;
+  const double a_panel = double(tile_m) * double(K) * 2.0, b_panel = double(tile_n) * double(K) * 2.0;
+  const double a_all = a_panel * double(num_m), b_all = b_panel * double(num_n);
+  inflight = inflight < 1 ? 1 : inflight;
+  double best = -1.0;
+  int choice = 16;
+  for (int64_t nb = 1; nb <= num_n; ++nb) {  // N-bands
+    const double foot = double(nb) * b_panel + double((inflight + nb - 1) / nb + 1) * a_panel;
+    if (foot > budget) continue;  // the footprint is not monotonic in the width
+    const double traffic = b_all + double((num_n + nb - 1) / nb) * a_all;
+    if (best < 0 || traffic < best) best = traffic, choice = -int(nb);
+  }
+  for (int64_t mb = 1; mb <= num_m && mb <= 64; ++mb) {  // M-groups
+    const double foot = double(mb) * a_panel + double((inflight + mb - 1) / mb + 1) * b_panel;
+    if (foot > budget) continue;  // the footprint is not monotonic in the width
+    const double traffic = a_all + double((num_m + mb - 1) / mb) * b_all;
+    if (best < 0 || traffic < best) best = traffic, choice = int(mb);
+  }
+  return choice;
+}
+
 bool tc_shape_ok(const ks_matmul_args &a) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   return a.k % 8 == 0 && a.n % 8 == 0 && al(a.a) && al(a.b) && al(a.out) && a.m < (1LL << 31) &&
@@ -535,8 +589,9 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   const int64_t tiles = ((a.m + kBM - 1) / kBM) * ((a.n + BN - 1) / BN);
   const int sms = ks::sm_count();
   const int grid = int(tiles < sms ? tiles : sms);
+  const int raster = plan_raster(cfg.group_m, a.m, a.n, a.k, kBM, BN, grid);
   kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n),
-                                                int(a.k), cfg.group_m, b3d, ks::wait_ctx());
+                                                int(a.k), raster, b3d, ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
 
@@ -580,8 +635,9 @@ int launch_tc2(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_
   const int64_t tiles = ((a.m + 2 * kBM - 1) / (2 * kBM)) * ((a.n + BN - 1) / BN);
   const int pairs = int(tiles < pairs_max ? tiles : pairs_max);
   lc.gridDim = dim3(2 * unsigned(pairs));
+  const int raster = plan_raster(cfg.group_m, a.m, a.n, a.k, 2 * kBM, BN, pairs);
   e = cudaLaunchKernelEx(&lc, kern, ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n), int(a.k),
-                         cfg.group_m, ks::wait_ctx());
+                         raster, ks::wait_ctx());
   if (e != cudaSuccess) return ks::map_cuda(e);
   return ks::map_cuda(cudaGetLastError());
 }
@@ -657,8 +713,8 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
     ks::set_reason(reason, len, "matmul: acc_stages must be 1 or 2 (TMEM accumulator buffers)");
     return KS_ERR_INVALID_CONFIG;
   }
-  if (cfg->group_m < 1 || cfg->group_m > 64) {
-    ks::set_reason(reason, len, "matmul: group_m must be 1..64");
+  if (cfg->group_m < 0 || cfg->group_m > 64) {
+    ks::set_reason(reason, len, "matmul: group_m must be 0 (raster planned from the L2) or 1..64");
     return KS_ERR_INVALID_CONFIG;
   }
   const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages);

@@ -782,10 +782,63 @@ __global__ void __launch_bounds__(1024) layernorm_twopass_kernel(const uint16_t 
 // ===========================================================================
 // bias_gelu
 // ===========================================================================
+// ---- exact-erf GELU ---------------------------------------------------------
+// The reference (refs.py:59-63, bias_gelu_gen.cpp:114-118) computes, for a
+// bf16 value t,
+//   x = fp32(t * fp32(1/sqrt 2)),  e = fp32(erf(double(x))),
+//   y = bf16(fp32(fp32(0.5 t) * fp32(1 + e))).
+// t has only 65536 values, so the kernels evaluate this function exactly:
+// * 2^-9 <= |t| < 8 (3072 codes): a table of the reference's own outputs,
+//   built at kernel start from double-precision erf (the erf values lie at
+//   least 1e5 double ulps from every fp32 rounding midpoint, so any erf
+//   accurate to a few double ulps rounds to the reference's e);
+// * |t| < 2^-9: |0.5 t e| is below half a bf16 ulp of 0.5 t, so y = 0.5 t;
+// * |t| >= 8 (and inf, NaN): e rounds to +-1, so y = t for t > 0 and
+//   0.5 t * 0 (= -0, or NaN for -inf and NaN) otherwise.
+// tests/test_gelu_erf_cpu.py checks these three rules against the reference
+// for all 65536 codes; the GPU tests check the kernels bit for bit.
+constexpr uint32_t kGeluTabLo = 0x3B00u;  // bf16 bits of 2^-9
+constexpr uint32_t kGeluTabHi = 0x4100u;  // bf16 bits of 8
+constexpr int kGeluTabN = int(kGeluTabHi - kGeluTabLo);  // 1536 magnitudes
+
+// The reference formula for bf16 bits tb (slow: one double erf).
+KS_DEV uint32_t gelu_erf_formula(uint32_t tb) {
+  const float t = __uint_as_float(tb << 16);
+  const float x = __fmul_rn(t, 0.70710678118654752f);
+  const float e = __double2float_rn(erf(double(x)));
+  return ks_f32_to_bf16(__fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.f, e)));
+}
+
+// Table word for magnitude code lo + i: GELU of +|t| in the low half, of -|t|
+// in the high half.  One erf serves both signs: x(-t) = -x(t) and the
+// rounding to fp32 is symmetric, so e(-t) = -e(t) exactly.
+KS_DEV uint32_t gelu_erf_table_word(int i) {
+  const float t = __uint_as_float((kGeluTabLo + uint32_t(i)) << 16);  // +|t|
+  const float x = __fmul_rn(t, 0.70710678118654752f);
+  const float e = __double2float_rn(erf(double(x)));
+  const float h = __fmul_rn(0.5f, t);
+  const uint32_t pos = ks_f32_to_bf16(__fmul_rn(h, __fadd_rn(1.f, e)));
+  const uint32_t neg = ks_f32_to_bf16(__fmul_rn(-h, __fadd_rn(1.f, -e)));
+  return pos | (neg << 16);
+}
+
+KS_DEV uint32_t gelu_erf_bits(const uint32_t *tab, uint32_t tb) {
+  const uint32_t mag = tb & 0x7fffu;
+  const uint32_t i = mag - kGeluTabLo;  // wraps below the table
+  if (i < uint32_t(kGeluTabN)) return (tab[i] >> ((tb >> 11) & 16u)) & 0xffffu;  // the sign picks the half
+  const float t = __uint_as_float(tb << 16);
+  return ks_f32_to_bf16(mag < kGeluTabLo ? 0.5f * t : (t > 0.f ? t : t * 0.f));
+}
+
+// GELU of both bf16 halves of a word.
+KS_DEV uint32_t gelu_erf_pair(const uint32_t *tab, uint32_t t2) {
+  return gelu_erf_bits(tab, t2 & 0xffffu) | (gelu_erf_bits(tab, t2 >> 16) << 16);
+}
+
+// Scalar form for the generic kernels (no table): the reference formula on
+// the rounded value, exact as well.
 KS_DEV float gelu_erf(float t) {
-  // 0.5 t (1 + erf(t/sqrt2)): erf rounded to fp32 before the add, as the
-  // reference does (refs.py:59-63).
-  return 0.5f * t * (1.f + erff(t * 0.70710678118654752f));
+  return ks_bf16_to_f32(uint16_t(gelu_erf_formula(ks_f32_to_bf16(t))));
 }
 KS_DEV float gelu_tanh(float t) {
   // 0.5 t (1 + tanh(u)) = t * sigmoid(2u), u = sqrt(2/pi) (t + 0.044715 t^3).
@@ -882,6 +935,52 @@ __global__ void __launch_bounds__(1024) bias_gelu_v8_kernel(const uint16_t *__re
         outw[h] = ks_pack_bf16x2(g0, g1);
       }
       __stcs(reinterpret_cast<uint4 *>(y + (r + u) * cols + c * 8), make_uint4(outw[0], outw[1], outw[2], outw[3]));
+    }
+  }
+}
+
+// Exact-erf GELU, 8-wide: each CTA first builds the 6 KB table of the
+// reference's outputs in shared memory, then walks row groups of
+// `rows_per_group` rows with a grid stride over blockIdx.y (a resident grid,
+// so the table is built once per CTA).  Each element is one shared-memory
+// lookup (rare codes outside the table take the two closed-form rules).
+template <int UNROLL>
+__global__ void __launch_bounds__(1024) bias_gelu_erf_v8_kernel(const uint16_t *__restrict__ x,
+                                                                const uint16_t *__restrict__ bias,
+                                                                uint16_t *__restrict__ y, int64_t total,
+                                                                int64_t cols, int64_t rows, int rows_per_group) {
+  __shared__ uint32_t tab[kGeluTabN];
+  for (int i = threadIdx.x; i < kGeluTabN; i += blockDim.x) tab[i] = gelu_erf_table_word(i);
+  __syncthreads();
+  const int64_t nvec = cols / 8;
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= nvec) return;
+  const uint4 bw = __ldg(reinterpret_cast<const uint4 *>(bias) + c);
+  const __nv_bfloat162 bb[4] = {as_bf162(bw.x), as_bf162(bw.y), as_bf162(bw.z), as_bf162(bw.w)};
+  const int64_t groups = (rows + rows_per_group - 1) / rows_per_group;
+  for (int64_t g = blockIdx.y; g < groups; g += gridDim.y) {
+    const int64_t r0 = g * rows_per_group;
+    const int64_t r1 = min(rows, r0 + rows_per_group);
+    for (int64_t r = r0; r < r1; r += UNROLL) {
+      uint4 w[UNROLL];
+      bool ok[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int64_t off = (r + u) * cols + c * 8;
+        ok[u] = (r + u < r1) && (off + 8 <= total);
+        if (ok[u]) w[u] = __ldcs(reinterpret_cast<const uint4 *>(x + off));
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        if (!ok[u]) continue;
+        const uint32_t in[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+        uint32_t outw[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h)  // t = bf16(x + bias): the bf16x2 add rounds the exact sum once
+          outw[h] = gelu_erf_pair(tab, as_u32(__hadd2(as_bf162(in[h]), bb[h])));
+        __stcs(reinterpret_cast<uint4 *>(y + (r + u) * cols + c * 8),
+               make_uint4(outw[0], outw[1], outw[2], outw[3]));
+      }
     }
   }
 }
@@ -1303,7 +1402,16 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
   const int64_t rows = (a.total + a.cols - 1) / a.cols;
   const int64_t nvec = a.cols / VEC;
   dim3 grid(unsigned((nvec + cfg.block - 1) / cfg.block), unsigned((rows + kBgRowsPerCta - 1) / kBgRowsPerCta));
-  if constexpr (VEC == 8)
+  if constexpr (VEC == 8 && GELU == KS_GELU_ERF) {
+    // resident grid over row groups: the table is built once per CTA
+    auto k = bias_gelu_erf_v8_kernel<4>;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, cfg.block, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    const int64_t resident = int64_t(per_sm) * ks::sm_count();
+    const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(grid.y, resident / std::max<int64_t>(1, grid.x)));
+    k<<<dim3(grid.x, unsigned(gy)), cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
+  } else if constexpr (VEC == 8)
     bias_gelu_v8_kernel<GELU, 4><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
   else
     bias_gelu_kernel<VEC, GELU, bg_unroll<VEC>()><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows,

@@ -11,6 +11,7 @@ from __future__ import annotations
 import itertools
 import os
 
+import ml_dtypes
 import numpy as np
 import pytest
 
@@ -217,6 +218,38 @@ def test_bias_gelu_erf_golden_all_configs(ks, path):
         assert_bf16_close(y, fx["expected"], gate=True)
         ran += 1
     assert ran > 0
+
+
+def _same_bf16_bits(a, b):
+    a, b = np.asarray(a).view(np.uint16), np.asarray(b).view(np.uint16)
+    fa = a.view(ml_dtypes.bfloat16).astype(np.float32)
+    fb = b.view(ml_dtypes.bfloat16).astype(np.float32)
+    return (a == b) | (np.isnan(fa) & np.isnan(fb))
+
+
+@pytest.mark.parametrize("vec", [8, 4, 2, 1])
+@pytest.mark.parametrize("block", [128, 1024])
+def test_bias_gelu_erf_bit_exact_every_bf16_code(ks, vec, block):
+    """The exact-erf GELU equals the reference bit for bit on all 65536 bf16
+    inputs (zeros, subnormals, infinities and NaN included; NaN compares as
+    NaN): t = x + 0 runs every code through the table and both closed forms."""
+    N, ops = ks
+    x = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16).view(ml_dtypes.bfloat16).reshape(64, 1024)
+    bias = np.zeros(1024, dtype=ml_dtypes.bfloat16)
+    cfg = N.BiasGeluConfig(block, vec, N.KS_GELU_ERF)
+    y = to_numpy(ops.bias_gelu(to_torch(x), to_torch(bias), gelu="erf", cfg=cfg))
+    with np.errstate(invalid="ignore"):
+        exp = orf.bias_gelu(x, bias)
+    assert _same_bf16_bits(y, exp).all(), int((~_same_bf16_bits(y, exp)).sum())
+
+
+def test_bias_gelu_erf_bit_exact_baseline_rows(ks):
+    """C3b rows with the reference's erf GELU: bit-identical to the oracle."""
+    _, ops = ks
+    shape = (16384, 16384)
+    inp = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=0, nrows=256)
+    y = to_numpy(ops.bias_gelu(to_torch(inp["x"]), to_torch(inp["bias"]), gelu="erf"))
+    assert _same_bf16_bits(y, orf.bias_gelu(inp["x"], inp["bias"])).all()
 
 
 @pytest.mark.parametrize("gelu", ["erf", "tanh"])
