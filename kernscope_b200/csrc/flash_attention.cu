@@ -530,6 +530,382 @@ __global__ void __launch_bounds__(kThreads2, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Two Q tiles per CTA with S in 64-key slots (config tile_m 256, tile_n 64).
+//
+// In the kernel above each tile computes S for 128 keys into the TMEM that
+// P of the previous 128 keys occupies, so a tile's chain per K/V tile is
+// softmax -> P V -> next Q K^T -> softmax, and the tensor core waits out the
+// hand-over.  Here each tile's 128 S columns are two 64-column slots and
+// every 64-key half-block is one online-softmax step (its own row max and
+// rescale check, P written over its slot, O += P V with K = 64).  The next
+// Q K^T of a slot is issued as soon as P V has read that slot, so it runs
+// while the softmax works on the other slot: the tile's chain per half-block
+// is one softmax step plus the hand-over, and the MMAs fill the gaps.
+//
+// TMEM: tile g's slots at columns [128 g, 128 g + 64) and [128 g + 64,
+// 128 g + 128), O_g at [256 + 128 g, 256 + 128 g + 128).  Half-step h of a
+// tile covers keys [64 h, 64 h + 64) of K/V tile h / 2 and uses slot h % 2.
+// K and V stages are released separately (K after the last Q K^T reading
+// it, two half-steps before V), so the loads run further ahead.  A rescale
+// of O at step h waits for the tile's P V of step h - 1 (barrier pv_done).
+// ---------------------------------------------------------------------------
+template <int D>
+struct FaRingLayout {
+  static constexpr uint32_t kTB = tile_bytes<D>();
+  static constexpr uint32_t q_off = 0;                      // Q0, Q1
+  static constexpr uint32_t k_off = q_off + 2 * kTB;        // K[stages]
+  static constexpr uint32_t v_off = k_off + kStages * kTB;  // V[stages]
+  static constexpr uint32_t bar_off = v_off + kStages * kTB;
+  // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2][2], p_full[2][2],
+  // pv_done[2], o_full[2], o_empty[2], drain
+  static constexpr uint32_t n_bars = 2 + 4 * kStages + 4 + 4 + 2 + 2 + 2 + 1;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
+  static constexpr uint32_t bytes = misc_off + 16;
+  static constexpr uint32_t smem_request = bytes + 1024;
+};
+
+// S(slot) = Q_g K_half^T: M=128, N=64 keys, K=d in steps of 16.  The K
+// half-tile starts 64 rows (8192 bytes, eight 1024-byte swizzle groups) into
+// each 64-column box.
+template <int D>
+KS_DEV void issue_s_half(uint32_t d_tmem, uint32_t q_addr, uint32_t k_half_addr) {
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, 64, false, false);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+    ks_umma_ss(d_tmem, ks_umma_desc_sw128(q_addr + off, 16, 1024),
+               ks_umma_desc_sw128(k_half_addr + off, 16, 1024), idesc, kk > 0);
+  }
+}
+
+// O_g (+)= P(slot) V_half: M=128, N=d, K=64 keys in 4 steps of 16; P is the
+// slot's first 32 columns (two bf16 per column), V_half starts 64 key-rows
+// (8192 bytes) into the MN-major tile.
+template <int D>
+KS_DEV void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_half_addr, bool accumulate) {
+  constexpr uint32_t idesc = ks_idesc_bf16_f32(128, D, false, true);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    ks_umma_ts(o_tmem, p_tmem + kk * 8, ks_umma_desc_sw128(v_half_addr + kk * 2048, kBox, 1024), idesc,
+               accumulate || kk > 0);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads2, 1)
+    fa_ring_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
+                   int n_bh, float scale_log2, int causal, KsWait wait) {
+  using L = FaRingLayout<D>;
+  constexpr uint32_t kTB = L::kTB;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ks_smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off);
+  uint64_t *q_full = bars;
+  uint64_t *q_empty = bars + 1;
+  uint64_t *k_full = bars + 2;
+  uint64_t *k_empty = k_full + kStages;
+  uint64_t *v_full = k_empty + kStages;
+  uint64_t *v_empty = v_full + kStages;
+  uint64_t *s_full = v_empty + kStages;  // [tile][slot]
+  uint64_t *p_full = s_full + 4;         // [tile][slot]
+  uint64_t *pv_done = p_full + 4;
+  uint64_t *o_full = pv_done + 2;
+  uint64_t *o_empty = o_full + 2;
+  uint64_t *drain = o_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qb = (nq + 2 * kTile - 1) / (2 * kTile);
+  const int num_items = num_qb * n_bh;
+  const int cta = int(blockIdx.x), G = int(gridDim.x);
+
+  if (threadIdx.x == 0) {
+    ks_mbar_init(q_full, 1);
+    ks_mbar_init(q_empty, 1);
+    for (int s = 0; s < kStages; ++s) {
+      ks_mbar_init(k_full + s, 1);
+      ks_mbar_init(k_empty + s, 1);
+      ks_mbar_init(v_full + s, 1);
+      ks_mbar_init(v_empty + s, 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      ks_mbar_init(s_full + i, 1);
+      ks_mbar_init(p_full + i, 4);
+    }
+    for (int g = 0; g < 2; ++g) {
+      ks_mbar_init(pv_done + g, 1);
+      ks_mbar_init(o_full + g, 1);
+      ks_mbar_init(o_empty + g, 4);
+    }
+    ks_mbar_init(drain, 1);
+    *abort = 0;
+    ks_fence_mbar_init();
+    ks_prefetch_tmap(&tm_q);
+    ks_prefetch_tmap(&tm_k);
+    ks_prefetch_tmap(&tm_v);
+  }
+  if (warp == 9) {
+    ks_tmem_alloc(tmem_slot, 512);
+    ks_tmem_relinquish();
+  }
+  ks_tc_fence_before();
+  __syncthreads();
+  ks_tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- producer
+        uint8_t *qs = smem + L::q_off;
+        uint32_t k_armed = 0, k_par = 0, v_armed = 0, v_par = 0;
+        int gj = 0, q_loads = 0;
+        bool ok = true;
+        FaItem it;
+        for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+          if (r > 0 && !ks_mbar_wait(q_empty, (r - 1) & 1, abort, wait)) break;
+          ks_mbar_arrive_expect_tx(q_full, 2 * kTB);
+          for (int g = 0; g < 2; ++g)
+            for (int h = 0; h < D / 64; ++h)
+              ks_tma_load_3d(qs + g * kTB + h * kBox, &tm_q, q_full, h * 64, it.q0 + g * kTile, it.bh);
+          ++q_loads;
+          for (int j = 0; j < it.n_kv; ++j, ++gj) {
+            const int st = gj % kStages;
+            const uint32_t ph = (gj / kStages) & 1;
+            if (!ks_mbar_wait(k_empty + st, ph ^ 1u, abort, wait)) {
+              ok = false;
+              break;
+            }
+            ks_mbar_arrive_expect_tx(k_full + st, kTB);
+            for (int h = 0; h < D / 64; ++h)
+              ks_tma_load_3d(smem + L::k_off + st * kTB + h * kBox, &tm_k, k_full + st, h * 64, j * kTile, it.bh);
+            k_armed |= 1u << st;
+            k_par = (k_par & ~(1u << st)) | (ph << st);
+            if (!ks_mbar_wait(v_empty + st, ph ^ 1u, abort, wait)) {
+              ok = false;
+              break;
+            }
+            ks_mbar_arrive_expect_tx(v_full + st, kTB);
+            for (int h = 0; h < D / 64; ++h)
+              ks_tma_load_3d(smem + L::v_off + st * kTB + h * kBox, &tm_v, v_full + st, h * 64, j * kTile, it.bh);
+            v_armed |= 1u << st;
+            v_par = (v_par & ~(1u << st)) | (ph << st);
+          }
+        }
+        // teardown: the loads issued above have landed
+        if (q_loads > 0) ks_mbar_wait(q_full, (q_loads - 1) & 1, nullptr, wait);
+        for (int s = 0; s < kStages; ++s) {
+          if (k_armed & (1u << s)) ks_mbar_wait(k_full + s, (k_par >> s) & 1u, nullptr, wait);
+          if (v_armed & (1u << s)) ks_mbar_wait(v_full + s, (v_par >> s) & 1u, nullptr, wait);
+        }
+      }
+    } else if (warp == 9) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- MMA issuer
+        const uint32_t q_addr = ks_smem_u32(smem + L::q_off);
+        const uint32_t k_addr = ks_smem_u32(smem + L::k_off);
+        const uint32_t v_addr = ks_smem_u32(smem + L::v_off);
+        int gj = 0;                     // K/V tiles consumed so far (ring position)
+        uint32_t par0 = 0, par1 = 0;    // p_full phase parities of tile 0 / 1, bit = slot
+        bool ok = true;
+        FaItem it;
+        for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+          const int H0 = 2 * it.n_t0, H1 = 2 * it.n_kv;  // half-steps per tile; H1 >= H0
+          ok = false;
+          if (!ks_mbar_wait(q_full, r & 1, abort, wait) ||
+              !ks_mbar_wait(k_full + gj % kStages, (gj / kStages) & 1, abort, wait))
+            break;
+          ks_tc_fence_after();
+          // prologue: both slots of both tiles from K/V tile 0
+#pragma unroll
+          for (int g = 0; g < 2; ++g)
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {  // H0, H1 >= 2
+              issue_s_half<D>(tmem + g * 128 + s * 64, q_addr + g * kTB, k_addr + (gj % kStages) * kTB + s * 8192);
+              ks_umma_commit(s_full + 2 * g + s);
+            }
+          ks_umma_commit(k_empty + gj % kStages);  // K tile 0 is fully read
+          if (H1 <= 2) ks_umma_commit(q_empty);     // that was the item's last read of Q
+          ok = true;
+          for (int h = 0; h < H1 && ok; ++h) {
+            const int half = h & 1;
+            const int jj = gj + (h >> 1);  // ring position of this step's K/V tile
+            const int st = jj % kStages;
+            const int jn = jj + 1, stn = jn % kStages;
+            ok = false;
+            if (half == 0 && !ks_mbar_wait(v_full + st, (jj / kStages) & 1, abort, wait)) break;
+            // this step's Q K^T (half-step h + 2) reads K tile jn, loaded three half-steps ago
+            if (h + 2 < H1 && !ks_mbar_wait(k_full + stn, (jn / kStages) & 1, abort, wait)) break;
+            ks_tc_fence_after();
+            // one half-step of tile g: O_g += P V, then the slot's next Q K^T
+            // (half-step h + 2 reads K/V tile jn); false on a failed wait
+            auto step = [&](int g, int hg, uint32_t &uses) -> bool {
+              if (h >= hg) return true;
+              // the item's first P V overwrites O: the previous epilogue must have read it
+              if (h == 0 && r > 0 && !ks_mbar_wait(o_empty + g, (r - 1) & 1, abort, wait)) return false;
+              if (!ks_mbar_wait(p_full + 2 * g + half, (uses >> half) & 1u, abort, wait)) return false;
+              uses ^= 1u << half;
+              ks_tc_fence_after();
+              issue_pv_half<D>(tmem + 256 + g * 128, tmem + g * 128 + half * 64, v_addr + st * kTB + half * 8192,
+                               h > 0);
+              ks_umma_commit(pv_done + g);
+              if (h + 1 == hg) ks_umma_commit(o_full + g);
+              if (h + 2 < hg) {
+                issue_s_half<D>(tmem + g * 128 + half * 64, q_addr + g * kTB, k_addr + stn * kTB + half * 8192);
+                ks_umma_commit(s_full + 2 * g + half);
+              }
+              return true;
+            };
+            if (!step(0, H0, par0) || !step(1, H1, par1)) break;
+            if (half == 1) {
+              ks_umma_commit(v_empty + st);                                 // V tile jj fully read
+              if ((h >> 1) + 1 < it.n_kv) ks_umma_commit(k_empty + stn);  // so is K tile jn
+            }
+            if (h + 3 == H1) ks_umma_commit(q_empty);  // the item's last Q K^T was just issued
+            ok = true;
+          }
+          gj += it.n_kv;
+        }
+        ks_umma_commit(drain);
+        ks_mbar_wait(drain, 0, nullptr, wait);
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    // ------------------------------------------------------------ softmax
+    const int g = warp >> 2;         // Q tile of this warpgroup
+    const int qd = warp & 3;         // TMEM lane quadrant
+    const int row = qd * 32 + lane;  // row within the tile = TMEM lane
+    const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t s_col = g * 128, o_col = 256 + g * 128;
+    uint32_t spar = 0;  // s_full phase parity per slot (bit = slot), over all items
+    int pv_base = 0;    // P V steps of this tile before the current item
+    bool ok = true;
+    FaItem it;
+    for (int r = 0; ok && fa_item(r, cta, G, num_items, num_qb, n_bh, nq, nk, causal, it); ++r) {
+      const int qrow = it.q0 + g * kTile + row;
+      float m = -INFINITY, l = 0.f;
+      const int Hg = 2 * (g == 0 ? it.n_t0 : it.n_kv);
+      for (int h = 0; h < Hg; ++h) {
+        const int slot = h & 1;
+        if (!ks_mbar_wait(s_full + 2 * g + slot, (spar >> slot) & 1u, abort, wait)) {
+          ok = false;
+          break;
+        }
+        spar ^= 1u << slot;
+        ks_tc_fence_after();
+        uint32_t rr[64];
+        ks_tmem_ld32_at<0>(lane_addr + s_col + slot * 64, rr);
+        ks_tmem_ld32_at<32>(lane_addr + s_col + slot * 64 + 32, rr);
+        ks_tmem_wait_ld();
+        const int kv0 = h * 64;
+        int lim = nk - kv0;  // valid keys of this half-block for this row
+        if (causal) lim = min(lim, qrow - kv0 + 1);
+        const bool full_block = __all_sync(0xffffffffu, lim >= 64);
+        if (!full_block) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= lim) rr[c] = 0xff800000u;  // -inf
+        }
+        float mm[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mm[u] = max3(__uint_as_float(rr[u]), __uint_as_float(rr[u + 4]), __uint_as_float(rr[u + 8]));
+#pragma unroll
+        for (int c = 12; c < 60; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mm[u] = max3(mm[u], __uint_as_float(rr[c + u]), __uint_as_float(rr[c + 4 + u]));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mm[u] = fmaxf(mm[u], __uint_as_float(rr[60 + u]));
+        const float mx = fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3]));
+        const float m_new = fmaxf(m, mx * scale_log2);
+        const bool grow = m_new > m + 8.f;  // also true on the first finite max
+        if (h > 0 && __any_sync(0xffffffffu, grow)) {
+          // O must hold every earlier P V of this item before it is rescaled
+          if (!ks_mbar_wait(pv_done + g, (pv_base + h - 1) & 1, abort, wait)) {
+            ok = false;
+            break;
+          }
+          ks_tc_fence_after();
+          const float alpha = grow ? ex2(m - m_new) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+            ks_tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(lane_addr + o_col + c * 32, o);
+          }
+          ks_tmem_wait_st();
+        }
+        if (grow) {
+          l *= ex2(m - m_new);
+          m = m_new;
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        F2 rsum[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+        const F2 sc2{scale_log2, scale_log2}, nm2{neg_m, neg_m};
+        uint32_t p[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const F2 x = fma2(F2{__uint_as_float(rr[2 * c]), __uint_as_float(rr[2 * c + 1])}, sc2, nm2);
+          const F2 e{ex2(x.x), ex2(x.y)};
+          rsum[c & 3] = add2(rsum[c & 3], e);
+          p[c] = ks_pack_bf16x2(e.x, e.y);
+        }
+        ks_tmem_st32_at<0>(lane_addr + s_col + slot * 64, p);
+        const F2 rs2 = add2(add2(rsum[0], rsum[1]), add2(rsum[2], rsum[3]));
+        l += rs2.x + rs2.y;
+        ks_tmem_wait_st();
+        ks_tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ks_mbar_arrive(p_full + 2 * g + slot);
+      }
+      pv_base += Hg;
+      // epilogue: O / l -> bf16 -> out[bh, qrow, :], then O is free again
+      if (!ok || !ks_mbar_wait(o_full + g, r & 1, abort, wait)) {
+        ok = false;
+        break;
+      }
+      ks_tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint16_t *dst = out + (int64_t(it.bh) * nq + qrow) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        ks_tmem_ld32(lane_addr + o_col + c * 32, o);
+        ks_tmem_wait_ld();
+        if (qrow < nq) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+            w.y = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+            w.z = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+            w.w = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+            *reinterpret_cast<uint4 *>(dst + c * 32 + v * 8) = w;
+          }
+        }
+      }
+      ks_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ks_mbar_arrive(o_empty + g);
+    }
+  }
+
+  ks_tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ks_tc_fence_after();
+    ks_tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // One 128-row Q tile per CTA with S double-buffered in TMEM.
 //
 // TMEM: S[0] columns [0,128), S[1] [128,256), O [256,384).  Because S(j+2)
@@ -895,12 +1271,13 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 template <int D>
 int launch_fwd(unsigned grid, cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
-               const ks_flash_attention_args &a, uint64_t bh, float scale_log2, int causal) {
-  cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(FaLayout<D>::smem_request));
+               const ks_flash_attention_args &a, uint64_t bh, float scale_log2, int causal, bool ring) {
+  auto kern = ring ? fa_ring_kernel<D> : fa_fwd_kernel<D>;
+  const uint32_t smem = ring ? FaRingLayout<D>::smem_request : FaLayout<D>::smem_request;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return ks::map_cuda(e);
-  fa_fwd_kernel<D><<<grid, kThreads2, FaLayout<D>::smem_request, st>>>(
-      tq, tk, tv, static_cast<uint16_t *>(a.out), int(a.nq), int(a.nk), int(bh), scale_log2, causal, ks::wait_ctx());
+  kern<<<grid, kThreads2, smem, st>>>(tq, tk, tv, static_cast<uint16_t *>(a.out), int(a.nq), int(a.nk), int(bh),
+                                      scale_log2, causal, ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
 
@@ -911,10 +1288,11 @@ extern "C" {
 int ks_flash_attention_validate(const ks_flash_attention_config *cfg, const ks_flash_attention_args *a,
                                 char *reason, size_t len) {
   if (!cfg || !a) return KS_ERR_INVALID_ARGS;
-  if ((cfg->tile_m != 128 && cfg->tile_m != 256) || cfg->tile_n != 128) {
+  if ((cfg->tile_m != 128 && cfg->tile_m != 256) ||
+      (cfg->tile_n != 128 && !(cfg->tile_n == 64 && cfg->tile_m == 256))) {
     ks::set_reason(reason, len,
                    "flash_attention: tile_m must be 128 or 256 (query rows per CTA: one or two UMMA M=128 "
-                   "tiles) and tile_n 128");
+                   "tiles) and tile_n 128 (keys per softmax step), or 64 with tile_m 256 (S in 64-key slots)");
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->stages != 2) {
@@ -987,8 +1365,9 @@ int ks_flash_attention_launch(const ks_flash_attention_config *cfg, const ks_fla
   const int64_t items = ((a->nq + 2 * kTile - 1) / (2 * kTile)) * int64_t(bh);
   const int sms = ks::sm_count();
   const unsigned grid = unsigned(items < sms ? items : sms);
-  return a->d == kD ? launch_fwd<kD>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal)
-                    : launch_fwd<64>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal);
+  const bool ring = cfg->tile_n == 64;
+  return a->d == kD ? launch_fwd<kD>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal, ring)
+                    : launch_fwd<64>(grid, st, tq, tk, tv, *a, bh, scale_log2, cfg->causal, ring);
 }
 
 }  // extern "C"

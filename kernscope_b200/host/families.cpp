@@ -434,9 +434,11 @@ class FlashFamily : public Family {
     // (tile_m 256: two query tiles per CTA) or two S tiles and one O tile
     // (tile_m 128: one query tile, S double-buffered); 128-key K/V tiles in a
     // 2-stage ring.
+    // tile_n 64: two query tiles with S in 64-key slots (one online-softmax
+    // step per 64 keys, the next Q K^T of a slot overlapping the other's softmax)
     std::vector<json> out;
-    for (int tm : {256, 128})
-      out.push_back(db::json::object({{"tile_m", json(tm)}, {"tile_n", json(128)}, {"stages", json(2)},
+    for (auto [tm, tn] : {std::pair{256, 128}, {128, 128}, {256, 64}})
+      out.push_back(db::json::object({{"tile_m", json(tm)}, {"tile_n", json(tn)}, {"stages", json(2)},
                                       {"causal", json(causal)}}));
     return out;
   }
@@ -926,9 +928,10 @@ std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProbl
   // tile_m 256: Q0, Q1 and a 2-stage K/V ring of 128 x d bf16 tiles;
   // tile_m 128: one Q tile, the K/V ring and the row-statistics exchange
   // (3 KB); plus barriers and alignment slack
+  // (tile_n 64, S in 64-key slots: the same tiles, 23 barriers)
   if (c.tile_m == 128) return 5 * 32768 + 3072 + 16 * 8 + 16 + 1024;
   const std::int64_t tile = p.d == 64 ? 16384 : 32768;
-  return 6 * tile + 16 * 8 + 16 + 1024;
+  return 6 * tile + (c.tile_n == 64 ? 23 : 16) * 8 + 16 + 1024;
 }
 
 LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) noexcept {

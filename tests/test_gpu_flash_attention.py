@@ -64,14 +64,20 @@ def _mh(shape, seed, scale=1.0):
     return mk(nq), mk(nk), mk(nk)
 
 
-@pytest.mark.parametrize("tile_m", [256, 128])
+# (tile_m, tile_n): two query tiles per CTA, one with S double-buffered, and
+# two query tiles with S in 64-key slots
+TILES = [(256, 128), (128, 128), (256, 64)]
+
+
+@pytest.mark.parametrize("tiles", TILES, ids=lambda t: f"m{t[0]}n{t[1]}")
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("shape", [(1, 1, 256, 256, 128), (2, 3, 384, 384, 128), (1, 2, 300, 300, 128),
-                                   (1, 1, 1, 1, 128), (1, 1, 129, 129, 128), (1, 1, 640, 640, 128)])
-def test_attention_multihead(ks, shape, causal, tile_m):
+                                   (1, 1, 1, 1, 128), (1, 1, 129, 129, 128), (1, 1, 640, 640, 128),
+                                   (1, 1, 192, 192, 128), (1, 2, 130, 130, 128)])
+def test_attention_multihead(ks, shape, causal, tiles):
     N, ops = ks
     q, k, v = _mh(shape, 7)
-    cfg = N.FlashAttentionConfig(tile_m, 128, 2, int(causal))
+    cfg = N.FlashAttentionConfig(tiles[0], tiles[1], 2, int(causal))
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
     _check_mh(o, q, k, v, causal)
 
@@ -80,52 +86,55 @@ def test_attention_multihead(ks, shape, causal, tile_m):
 @pytest.mark.parametrize("shape", [(1, 1, 256, 256, 64), (2, 3, 384, 384, 64), (1, 2, 300, 300, 64),
                                    (1, 1, 1, 1, 64), (1, 1, 129, 129, 64), (1, 2, 200, 520, 64),
                                    (1, 1, 520, 200, 64)])
-def test_attention_d64_tensor_cores(ks, shape, causal):
-    """d = 64 on the tcgen05 kernel (two query tiles per CTA): one 64-column
+@pytest.mark.parametrize("tile_n", [128, 64])
+def test_attention_d64_tensor_cores(ks, shape, causal, tile_n):
+    """d = 64 on the tcgen05 kernels (two query tiles per CTA): one 64-column
     box per tile, P V with N = 64."""
     N, ops = ks
     q, k, v = _mh(shape, 11)
-    cfg = N.FlashAttentionConfig(256, 128, 2, int(causal))
+    cfg = N.FlashAttentionConfig(256, tile_n, 2, int(causal))
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
     _check_mh(o, q, k, v, causal)
 
 
-def test_attention_d64_large_logits(ks):
+@pytest.mark.parametrize("tile_n", [128, 64])
+def test_attention_d64_large_logits(ks, tile_n):
     N, ops = ks
     q, k, v = _mh((1, 2, 512, 512, 64), 12, scale=4.0)
-    cfg = N.FlashAttentionConfig(256, 128, 2, 1)
+    cfg = N.FlashAttentionConfig(256, tile_n, 2, 1)
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=True, cfg=cfg))
     _check_mh(o, q, k, v, True)
 
 
-@pytest.mark.parametrize("tile_m", [256, 128])
+@pytest.mark.parametrize("tiles", TILES, ids=lambda t: f"m{t[0]}n{t[1]}")
 @pytest.mark.parametrize("shape", [(1, 2, 200, 520, 128), (1, 1, 520, 200, 128), (2, 1, 64, 1000, 64)])
-def test_attention_cross_lengths(ks, shape, tile_m):
+def test_attention_cross_lengths(ks, shape, tiles):
     N, ops = ks
     q, k, v = _mh(shape, 8)
-    cfg = N.FlashAttentionConfig(tile_m, 128, 2, 0)
+    cfg = N.FlashAttentionConfig(tiles[0], tiles[1], 2, 0)
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=False, cfg=cfg))
     _check_mh(o, q, k, v, False)
 
 
-@pytest.mark.parametrize("tile_m", [256, 128])
-def test_attention_large_logits(ks, tile_m):
+@pytest.mark.parametrize("tiles", TILES, ids=lambda t: f"m{t[0]}n{t[1]}")
+def test_attention_large_logits(ks, tiles):
     """Scores spread far apart force the running-max rescale of O."""
     N, ops = ks
     q, k, v = _mh((1, 2, 512, 512, 128), 9, scale=4.0)
-    cfg = N.FlashAttentionConfig(tile_m, 128, 2, 1)
+    cfg = N.FlashAttentionConfig(tiles[0], tiles[1], 2, 1)
     o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=True, cfg=cfg))
     _check_mh(o, q, k, v, True)
 
 
-def test_attention_c5_sampled(ks):
+@pytest.mark.parametrize("tile_n", [128, 64])
+def test_attention_c5_sampled(ks, tile_n):
     """C5: B8 H32 N8192 d128 causal, Q/K/V ~ N(0,1); heads (0,0) and (7,31)
     of the full launch checked against the oracle."""
-    _, ops = ks
+    N, ops = ks
     b, h, s, d = 8, 32, 8192, 128
     inp = oin.baseline_inputs("attention", (b, h, s, s, d), seed=4)
     q, k, v = (to_torch(inp[n].reshape(b, h, s, d)) for n in ("q", "k", "v"))
-    o = ops.flash_attention(q, k, v, causal=True)
+    o = ops.flash_attention(q, k, v, causal=True, cfg=N.FlashAttentionConfig(256, tile_n, 2, 1))
     for bi, hi in ((0, 0), (7, 31)):
         idx = bi * h + hi
         qi, ki, vi = inp["q"][idx], inp["k"][idx], inp["v"][idx]
@@ -142,3 +151,5 @@ def test_attention_invalid(ks):
     assert N.validate("flash_attention", N.FlashAttentionConfig(128, 128, 2, 1), a)[0] == 0
     assert N.validate("flash_attention", N.FlashAttentionConfig(256, 128, 2, 1), a)[0] == 0
     assert N.validate("flash_attention", N.FlashAttentionConfig(192, 128, 2, 1), a)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("flash_attention", N.FlashAttentionConfig(256, 64, 2, 1), a)[0] == 0
+    assert N.validate("flash_attention", N.FlashAttentionConfig(128, 64, 2, 1), a)[0] == N.KS_ERR_INVALID_CONFIG

@@ -49,7 +49,7 @@ def test_rowop_spaces_and_rejections():
     red = tune.query("enumerate", family="reduction", shape=[1 << 28])
     assert all(v["valid"] for v in red)
     fa = tune.query("enumerate", family="flash_attention", shape=[8, 32, 8192, 128], causal=True)
-    assert len(fa) == 2 and all(v["valid"] and v["symbol"].endswith("_causal") for v in fa)
+    assert len(fa) == 3 and all(v["valid"] and v["symbol"].endswith("_causal") for v in fa)
     assert {v["config"]["tile_m"] for v in fa} == {128, 256}
     v = tune.query("validate", family="softmax", shape=[4, 100], config={"block": 256, "vec_width": 8, "mode": "onepass"})
     assert not v["valid"] and "vec_width" in v["reason"]
