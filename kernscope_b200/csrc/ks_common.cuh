@@ -159,6 +159,25 @@ KS_DEV void ks_tma_load_3d(void *dst, const CUtensorMap *m, uint64_t *bar, int c
       : "memory");
 }
 
+// TMA store of a 2-D box from this CTA's shared memory (bulk-group
+// completion: commit, then wait_group.read before the buffer is rewritten and
+// wait_group 0 before exit).  Non-negative coordinates only; the innermost
+// coordinate times the element size is a multiple of 16 bytes.
+KS_DEV void ks_tma_store_2d(const CUtensorMap *m, const void *src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(ks_smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+KS_DEV void ks_bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most N committed bulk groups still reading their shared-memory source.
+template <int N>
+KS_DEV void ks_bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Every committed bulk group complete (its global writes done).
+KS_DEV void ks_bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, UMMA issue, commit, TMEM <-> register moves
 // ---------------------------------------------------------------------------

@@ -36,12 +36,18 @@ constexpr int kThreads = 192;              // 6 warps: producer, MMA, 4 x epilog
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB per stage
 constexpr uint32_t kBBoxBytes = kBK * 64 * 2;  // one B box: 64 K-rows x 64 N-cols = 8 KB
 
+// Epilogue staging for the TMA store of C: per epilogue warp two buffers of
+// [32 rows x 32 columns] bf16 (64-byte rows, 64-byte swizzle), 2 KB each.
+constexpr uint32_t kCBuf = 32 * 64;
+constexpr uint32_t kCStage = 4 * 2 * kCBuf;  // 4 warps x 2 buffers = 16 KB
+
 template <int BN, int STAGES, int ACC>
 struct MmLayout {
   static constexpr uint32_t b_bytes = kBK * BN * 2;
   static constexpr uint32_t a_off = 0;
   static constexpr uint32_t b_off = a_off + STAGES * kABytes;
-  static constexpr uint32_t bar_off = b_off + STAGES * b_bytes;
+  static constexpr uint32_t c_off = b_off + STAGES * b_bytes;  // 1024-aligned (stage sizes are multiples of 8 KB)
+  static constexpr uint32_t bar_off = c_off + kCStage;
   // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
   static constexpr uint32_t n_bars = 2 * STAGES + 2 * ACC + 1;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
@@ -82,7 +88,8 @@ KS_DEV void tile_coords(int t, int num_m, int num_n, int raster, int &tm, int &t
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     uint16_t *__restrict__ c, int M, int N, int K, int raster, int b3d, KsWait wait) {
+                     const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int raster, int b3d,
+                     KsWait wait) {
   using L = MmLayout<BN, STAGES, ACC>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
@@ -115,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ks_fence_mbar_init();
     ks_prefetch_tmap(&tma_a);
     ks_prefetch_tmap(&tma_b);
+    ks_prefetch_tmap(&tma_c);
   }
   if (warp == 1) {
     ks_tmem_alloc(tmem_slot, L::tmem_cols);
@@ -205,9 +213,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     ks_mbar_wait(drain, 0, nullptr, wait);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
+    // Each warp drains its 32 accumulator lanes (rows) 32 columns at a time:
+    // tcgen05.ld, round to bf16, write the [32 x 32] block into one of its two
+    // swizzled staging buffers, and lane 0 stores the block with TMA (the
+    // store clips rows >= M and columns >= N).  The accumulator is released
+    // as soon as its last columns are in registers.
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row_in_tile = q * 32 + lane;
+    uint8_t *stg = smem + L::c_off + (warp - 2) * 2 * kCBuf;
     int i = 0;
+    uint32_t nstore = 0;  // blocks this warp has stored (buffer = nstore & 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int acc = i % ACC;
       const uint32_t acc_phase = (i / ACC) & 1;
@@ -215,33 +229,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       ks_tc_fence_after();
       int tm, tn;
       tile_coords(t, num_m, num_n, raster, tm, tn);
-      const int64_t row = int64_t(tm) * kBM + row_in_tile;
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         ks_tmem_ld32(t_addr + cc * 32, r);
         ks_tmem_wait_ld();
-        const int col0 = tn * BN + cc * 32;
-        if (row < M && num_kb > 0) {
-          uint16_t *dst = c + row * N + col0;
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            if (col0 + v * 8 < N) {
-              uint4 w;
-              w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-              w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-              w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-              w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-              *reinterpret_cast<uint4 *>(dst + v * 8) = w;
-            }
-          }
+        if (cc + 1 == BN / 32) {  // the accumulator is free for the next tile's MMAs
+          ks_tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ks_mbar_arrive(tempty + acc);
         }
+        if (num_kb == 0) continue;  // K = 0 is written by the host (zeros)
+        uint8_t *buf = stg + (nstore & 1) * kCBuf;
+        if (lane == 0) ks_bulk_wait_read<1>();  // the store two blocks back has read this buffer
+        __syncwarp();
+        // row = lane: four 16-byte chunks, chunk v at position v ^ ((lane >> 1) & 3) (64-byte swizzle)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+          w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+          w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+          w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+          *reinterpret_cast<uint4 *>(buf + lane * 64 + ((v ^ ((lane >> 1) & 3)) * 16)) = w;
+        }
+        ks_fence_proxy_async();  // the generic-proxy writes are visible to the TMA store
+        __syncwarp();
+        if (lane == 0) {
+          ks_tma_store_2d(&tma_c, buf, tn * BN + cc * 32, tm * kBM + q * 32);
+          ks_bulk_commit_group();
+        }
+        ++nstore;
       }
-      ks_tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ks_mbar_arrive(tempty + acc);
     }
+    if (lane == 0) ks_bulk_wait_all();  // C is in global memory before the CTA exits
   }
 
   ks_tc_fence_before();
@@ -583,6 +605,11 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
                            uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KS_OK) return s;
   }
+  // C: [32 columns x 32 rows] boxes, 64-byte swizzle (the epilogue's staging layout)
+  CUtensorMap tc;
+  s = ks::encode_tmap_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, uint64_t(a.n), uint64_t(a.m),
+                         uint64_t(a.n) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (s != KS_OK) return s;
   auto kern = matmul_tc_kernel<BN, STAGES, ACC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
@@ -590,8 +617,8 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   const int sms = ks::sm_count();
   const int grid = int(tiles < sms ? tiles : sms);
   const int raster = plan_raster(cfg.group_m, a.m, a.n, a.k, kBM, BN, grid);
-  kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n),
-                                                int(a.k), raster, b3d, ks::wait_ctx());
+  kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, tc, int(a.m), int(a.n), int(a.k), raster, b3d,
+                                                ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
 
@@ -675,10 +702,12 @@ int launch_tc_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaS
 constexpr uint32_t kSmemLimit = 227 * 1024;
 
 // Per-CTA bytes: A ring + B ring (half of tile_n per CTA for the pair
-// kernel) + barriers + alignment slack.
+// kernel) + the C staging buffers of the one-CTA kernel's TMA-store
+// epilogue + barriers + alignment slack.
 uint32_t smem_for(int bm, int bn, int stages) {
   const uint32_t b_cols = bm == 256 ? uint32_t(bn / 2) : uint32_t(bn);
-  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + (2 * stages + 5) * 8 + 16 + 1024;
+  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + (bm == 128 ? kCStage : 0) +
+         (2 * stages + 5) * 8 + 16 + 1024;
 }
 
 }  // namespace
