@@ -139,6 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t armed = 0, armed_parity = 0;  // per-stage bits for the teardown wait
     bool ok = true;
+    // L2 policy per operand: the raster keeps one operand's panels for reuse
+    // (A with M-groups, B with N-bands) and streams the other past them
+    const uint64_t pol_keep = ks_policy_evict_last(), pol_stream = ks_policy_evict_first();
+    const uint64_t pol_a = raster > 0 ? pol_keep : pol_stream;
+    const uint64_t pol_b = raster > 0 ? pol_stream : pol_keep;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, num_m, num_n, raster, tm, tn);
@@ -150,14 +155,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *a_dst = smem + L::a_off + stage * kABytes;
         uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
         ks_mbar_arrive_expect_tx(full + stage, kABytes + L::b_bytes);
-        ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
+        ks_tma_load_2d_hint(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM, pol_a);
         if (b3d) {
           // one copy for all BN/64 column blocks (tensor map dims: 64 columns, K, N/64)
-          ks_tma_load_3d(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64));
+          ks_tma_load_3d_hint(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64), pol_b);
         } else {
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+            ks_tma_load_2d_hint(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK, pol_b);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
