@@ -4,8 +4,7 @@
 // tiles in shared memory and accumulates with scalar FMAs.  Here:
 //
 //   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256),
-//     raster grouped by `group_m` M-tiles for L2 reuse, or (group_m 0)
-//     planned from the L2 size: M-groups or B-resident N-bands;
+//     raster grouped by `group_m` M-tiles for L2 reuse;
 //   * warp 0 (one lane) is the TMA producer: per K-block of 64 it loads the
 //     A box [128 rows x 64 K] and BN/64 B boxes [64 K x 64 N], all with the
 //     128-byte swizzle, into a STAGES-deep shared-memory ring (full/empty
@@ -58,24 +57,7 @@ struct MmLayout {
                                         : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
 };
 
-// Tile t (of num_m x num_n) in raster order.  raster > 0: groups of
-// `raster` M-tiles, M fastest within a group, so each group streams all of B
-// once.  raster < 0: bands of -raster N-tiles, N fastest within a band, so a
-// band's B panels stay in L2 while every M-tile passes and A is streamed once
-// per band (the cheaper order when A is much larger than B).
-KS_DEV void tile_coords(int t, int num_m, int num_n, int raster, int &tm, int &tn) {
-  if (raster < 0) {
-    const int band = -raster;
-    const int per_band = band * num_m;
-    const int b = t / per_band;
-    const int first_n = b * band;
-    const int bn = min(num_n - first_n, band);
-    const int r = t - b * per_band;
-    tm = r / bn;
-    tn = first_n + r % bn;
-    return;
-  }
-  const int group_m = raster;
+KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &tn) {
   const int group_size = group_m * num_n;
   const int g = t / group_size;
   const int first_m = g * group_m;
@@ -88,7 +70,7 @@ KS_DEV void tile_coords(int t, int num_m, int num_n, int raster, int &tm, int &t
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int raster, int b3d,
+                     const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int group_m, int b3d,
                      KsWait wait) {
   using L = MmLayout<BN, STAGES, ACC>;
   extern __shared__ uint8_t smem_raw[];
@@ -139,14 +121,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t armed = 0, armed_parity = 0;  // per-stage bits for the teardown wait
     bool ok = true;
-    // L2 policy per operand: the raster keeps one operand's panels for reuse
-    // (A with M-groups, B with N-bands) and streams the other past them
-    const uint64_t pol_keep = ks_policy_evict_last(), pol_stream = ks_policy_evict_first();
-    const uint64_t pol_a = raster > 0 ? pol_keep : pol_stream;
-    const uint64_t pol_b = raster > 0 ? pol_stream : pol_keep;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, raster, tm, tn);
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait(empty + stage, phase ^ 1u, abort, wait)) {
           ok = false;
@@ -155,14 +132,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *a_dst = smem + L::a_off + stage * kABytes;
         uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
         ks_mbar_arrive_expect_tx(full + stage, kABytes + L::b_bytes);
-        ks_tma_load_2d_hint(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM, pol_a);
+        ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
         if (b3d) {
           // one copy for all BN/64 column blocks (tensor map dims: 64 columns, K, N/64)
-          ks_tma_load_3d_hint(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64), pol_b);
+          ks_tma_load_3d(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64));
         } else {
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            ks_tma_load_2d_hint(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK, pol_b);
+            ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -233,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ks_mbar_wait(tfull + acc, acc_phase, abort, wait)) break;
       ks_tc_fence_after();
       int tm, tn;
-      tile_coords(t, num_m, num_n, raster, tm, tn);
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
@@ -318,7 +295,7 @@ struct Mm2Layout {
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                      uint16_t *__restrict__ c, int M, int N, int K, int raster, KsWait wait) {
+                      uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
   using L = Mm2Layout<BN, STAGES, ACC>;
   constexpr int kPM = 2 * kBM;  // rows per pair tile
   extern __shared__ uint8_t smem_raw[];
@@ -373,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int t = pair; t < num_tiles && ok; t += num_pairs) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, raster, tm, tn);
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait_cluster(empty + stage, phase ^ 1u, abort, wait)) {
           ok = false;
@@ -463,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ks_mbar_wait_cluster(tfull + acc, acc_phase, abort, wait)) break;
       ks_tc_fence_after();
       int tm, tn;
-      tile_coords(t, num_m, num_n, raster, tm, tn);
+      tile_coords(t, num_m, num_n, group_m, tm, tn);
       const int64_t row = int64_t(tm) * kPM + row_in_tile;
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -549,42 +526,6 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(const uint16_t *__rest
     }
 }
 
-// The tile raster of a launch.  group_m > 0 is the configured M-group.
-// group_m == 0 plans from the L2: the in-flight tiles (one per CTA, or per
-// CTA pair) plus the panels kept for reuse must fit in ~70 % of the L2.
-//   * M-groups of mb tiles: A read once, B once per group;
-//   * N-bands of nb tiles: B read once, A once per band;
-// each with the widest group that fits, and the order with less modelled
-// DRAM traffic wins (65536 x 8192 x 8192: N-bands of 17 tiles, 2.1 GB of
-// reads, against 32 B streams with M-groups of 16).
-int plan_raster(int group_m, int64_t M, int64_t N, int64_t K, int tile_m, int tile_n, int64_t inflight) {
-  if (group_m > 0) return group_m;
-  int dev = 0, l2 = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) != cudaSuccess ||
-      l2 <= 0)
-    l2 = 126 << 20;
-  const double budget = 0.7 * double(l2);
-  const int64_t num_m = (M + tile_m - 1) / tile_m, num_n = (N + tile_n - 1) / tile_n;
-  const double a_panel = double(tile_m) * double(K) * 2.0, b_panel = double(tile_n) * double(K) * 2.0;
-  const double a_all = a_panel * double(num_m), b_all = b_panel * double(num_n);
-  inflight = inflight < 1 ? 1 : inflight;
-  double best = -1.0;
-  int choice = 16;
-  for (int64_t nb = 1; nb <= num_n; ++nb) {  // N-bands
-    const double foot = double(nb) * b_panel + double((inflight + nb - 1) / nb + 1) * a_panel;
-    if (foot > budget) continue;  // the footprint is not monotonic in the width
-    const double traffic = b_all + double((num_n + nb - 1) / nb) * a_all;
-    if (best < 0 || traffic < best) best = traffic, choice = -int(nb);
-  }
-  for (int64_t mb = 1; mb <= num_m && mb <= 64; ++mb) {  // M-groups
-    const double foot = double(mb) * a_panel + double((inflight + mb - 1) / mb + 1) * b_panel;
-    if (foot > budget) continue;  // the footprint is not monotonic in the width
-    const double traffic = a_all + double((num_m + mb - 1) / mb) * b_all;
-    if (best < 0 || traffic < best) best = traffic, choice = int(mb);
-  }
-  return choice;
-}
-
 bool tc_shape_ok(const ks_matmul_args &a) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   return a.k % 8 == 0 && a.n % 8 == 0 && al(a.a) && al(a.b) && al(a.out) && a.m < (1LL << 31) &&
@@ -621,8 +562,7 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   const int64_t tiles = ((a.m + kBM - 1) / kBM) * ((a.n + BN - 1) / BN);
   const int sms = ks::sm_count();
   const int grid = int(tiles < sms ? tiles : sms);
-  const int raster = plan_raster(cfg.group_m, a.m, a.n, a.k, kBM, BN, grid);
-  kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, tc, int(a.m), int(a.n), int(a.k), raster, b3d,
+  kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, tc, int(a.m), int(a.n), int(a.k), cfg.group_m, b3d,
                                                 ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
@@ -667,9 +607,8 @@ int launch_tc2(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_
   const int64_t tiles = ((a.m + 2 * kBM - 1) / (2 * kBM)) * ((a.n + BN - 1) / BN);
   const int pairs = int(tiles < pairs_max ? tiles : pairs_max);
   lc.gridDim = dim3(2 * unsigned(pairs));
-  const int raster = plan_raster(cfg.group_m, a.m, a.n, a.k, 2 * kBM, BN, pairs);
   e = cudaLaunchKernelEx(&lc, kern, ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n), int(a.k),
-                         raster, ks::wait_ctx());
+                         cfg.group_m, ks::wait_ctx());
   if (e != cudaSuccess) return ks::map_cuda(e);
   return ks::map_cuda(cudaGetLastError());
 }
@@ -747,8 +686,8 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
     ks::set_reason(reason, len, "matmul: acc_stages must be 1 or 2 (TMEM accumulator buffers)");
     return KS_ERR_INVALID_CONFIG;
   }
-  if (cfg->group_m < 0 || cfg->group_m > 64) {
-    ks::set_reason(reason, len, "matmul: group_m must be 0 (raster planned from the L2) or 1..64");
+  if (cfg->group_m < 1 || cfg->group_m > 64) {
+    ks::set_reason(reason, len, "matmul: group_m must be 1..64");
     return KS_ERR_INVALID_CONFIG;
   }
   const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages);

@@ -788,7 +788,7 @@ __global__ void __launch_bounds__(1024) layernorm_twopass_kernel(const uint16_t 
 //   x = fp32(t * fp32(1/sqrt 2)),  e = fp32(erf(double(x))),
 //   y = bf16(fp32(fp32(0.5 t) * fp32(1 + e))).
 // t has only 65536 values, so the kernels evaluate this function exactly:
-// * 2^-9 <= |t| < 8 (3072 codes): a table of the reference's own outputs,
+// * 2^-9 <= |t| < 8 (3072 codes): a 6 KB table of the reference's own outputs,
 //   built at kernel start from double-precision erf (the erf values lie at
 //   least 1e5 double ulps from every fp32 rounding midpoint, so any erf
 //   accurate to a few double ulps rounds to the reference's e);
@@ -809,30 +809,36 @@ KS_DEV uint32_t gelu_erf_formula(uint32_t tb) {
   return ks_f32_to_bf16(__fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.f, e)));
 }
 
-// Table word for magnitude code lo + i: GELU of +|t| in the low half, of -|t|
-// in the high half.  One erf serves both signs: x(-t) = -x(t) and the
-// rounding to fp32 is symmetric, so e(-t) = -e(t) exactly.
-KS_DEV uint32_t gelu_erf_table_word(int i) {
+// Table entries for magnitude code lo + i (i < kGeluTabN): GELU of +|t| at
+// [i], of -|t| at [kGeluTabN + i] (bf16 bits).  One erf serves both signs:
+// x(-t) = -x(t) and the rounding to fp32 is symmetric, so e(-t) = -e(t)
+// exactly.
+KS_DEV void gelu_erf_table_entries(uint16_t *tab, int i) {
   const float t = __uint_as_float((kGeluTabLo + uint32_t(i)) << 16);  // +|t|
   const float x = __fmul_rn(t, 0.70710678118654752f);
   const float e = __double2float_rn(erf(double(x)));
   const float h = __fmul_rn(0.5f, t);
-  const uint32_t pos = ks_f32_to_bf16(__fmul_rn(h, __fadd_rn(1.f, e)));
-  const uint32_t neg = ks_f32_to_bf16(__fmul_rn(-h, __fadd_rn(1.f, -e)));
-  return pos | (neg << 16);
+  tab[i] = ks_f32_to_bf16(__fmul_rn(h, __fadd_rn(1.f, e)));
+  tab[kGeluTabN + i] = ks_f32_to_bf16(__fmul_rn(-h, __fadd_rn(1.f, -e)));
 }
 
-KS_DEV uint32_t gelu_erf_bits(const uint32_t *tab, uint32_t tb) {
-  const uint32_t mag = tb & 0x7fffu;
-  const uint32_t i = mag - kGeluTabLo;  // wraps below the table
-  if (i < uint32_t(kGeluTabN)) return (tab[i] >> ((tb >> 11) & 16u)) & 0xffffu;  // the sign picks the half
+// The codes outside the table (about 0.1 % of N(0,1) inputs), kept out of
+// line so the table lookup stays a few instructions.
+__device__ __noinline__ uint32_t gelu_erf_edge(uint32_t tb) {
   const float t = __uint_as_float(tb << 16);
-  return ks_f32_to_bf16(mag < kGeluTabLo ? 0.5f * t : (t > 0.f ? t : t * 0.f));
+  return ks_f32_to_bf16((tb & 0x7fffu) < kGeluTabLo ? 0.5f * t : (t > 0.f ? t : t * 0.f));
+}
+
+// GELU of the bf16 value with bits tb (low 16 bits).
+KS_DEV uint32_t gelu_erf_bits(const uint16_t *tab, uint32_t tb) {
+  const uint32_t i = (tb & 0x7fffu) - kGeluTabLo;  // wraps below the table
+  if (i < uint32_t(kGeluTabN)) return tab[i + (tb >> 15) * uint32_t(kGeluTabN)];
+  return gelu_erf_edge(tb);
 }
 
 // GELU of both bf16 halves of a word.
-KS_DEV uint32_t gelu_erf_pair(const uint32_t *tab, uint32_t t2) {
-  return gelu_erf_bits(tab, t2 & 0xffffu) | (gelu_erf_bits(tab, t2 >> 16) << 16);
+KS_DEV uint32_t gelu_erf_pair(const uint16_t *tab, uint32_t t2) {
+  return __byte_perm(gelu_erf_bits(tab, t2 & 0xffffu), gelu_erf_bits(tab, t2 >> 16), 0x5410);
 }
 
 // Scalar form for the generic kernels (no table): the reference formula on
@@ -949,8 +955,8 @@ __global__ void __launch_bounds__(1024) bias_gelu_erf_v8_kernel(const uint16_t *
                                                                 const uint16_t *__restrict__ bias,
                                                                 uint16_t *__restrict__ y, int64_t total,
                                                                 int64_t cols, int64_t rows, int rows_per_group) {
-  __shared__ uint32_t tab[kGeluTabN];
-  for (int i = threadIdx.x; i < kGeluTabN; i += blockDim.x) tab[i] = gelu_erf_table_word(i);
+  __shared__ uint16_t tab[2 * kGeluTabN];
+  for (int i = threadIdx.x; i < kGeluTabN; i += blockDim.x) gelu_erf_table_entries(tab, i);
   __syncthreads();
   const int64_t nvec = cols / 8;
   const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;

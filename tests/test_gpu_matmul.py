@@ -138,24 +138,3 @@ def test_matmul_invalid_configs(ks):
     assert N.validate("matmul", N.MatmulConfig(128, 96, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(256, 64, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 6, 2, 8), 64, 64, 64)[0] == 0
-
-
-@pytest.mark.parametrize("shape", [(4096, 8192, 1024), (3000, 2056, 512), (65536, 1024, 256)])
-@pytest.mark.parametrize("tile_m", [128, 256])
-def test_matmul_planned_raster_bit_identical(ks, shape, tile_m):
-    """group_m 0 (raster planned from the L2: M-groups or N-bands) visits
-    the same tiles in another order; every tile is computed the same way, so
-    C is bit-identical to the fixed group-16 raster."""
-    import torch
-
-    N, ops = ks
-    m, n, k = shape
-    g = torch.Generator(device="cuda")
-    g.manual_seed(5)
-    a = (torch.randn((m, k), generator=g, device="cuda") / k ** 0.5).bfloat16()
-    b = (torch.randn((k, n), generator=g, device="cuda") / k ** 0.5).bfloat16()
-    bn, st = 256, (4 if tile_m == 128 else 5)
-    c16 = ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, bn, 64, st, 2, 16))
-    c0 = ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, bn, 64, st, 2, 0))
-    torch.cuda.synchronize()
-    assert torch.equal(c0, c16)
