@@ -281,7 +281,8 @@ struct Mm2Layout {
   static constexpr uint32_t b_bytes = kBK * (BN / 2) * 2;  // this CTA's half of a B stage
   static constexpr uint32_t a_off = 0;
   static constexpr uint32_t b_off = a_off + STAGES * kABytes;
-  static constexpr uint32_t bar_off = b_off + STAGES * b_bytes;
+  static constexpr uint32_t c_off = b_off + STAGES * b_bytes;  // C staging, 1024-aligned
+  static constexpr uint32_t bar_off = c_off + kCStage;
   // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
   static constexpr uint32_t n_bars = 2 * STAGES + 2 * ACC + 1;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
@@ -295,7 +296,7 @@ struct Mm2Layout {
 template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                      uint16_t *__restrict__ c, int M, int N, int K, int group_m, KsWait wait) {
+                      const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int group_m, KsWait wait) {
   using L = Mm2Layout<BN, STAGES, ACC>;
   constexpr int kPM = 2 * kBM;  // rows per pair tile
   extern __shared__ uint8_t smem_raw[];
@@ -430,10 +431,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     ks_mbar_wait(drain, 0, nullptr, wait);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
+    // Same TMA-store epilogue as the one-CTA kernel, over this CTA's 128
+    // rows of the 256-row pair tile.
     const uint32_t tempty_even = ks_mapa(ks_smem_u32(tempty), 0);
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row_in_tile = int(rank) * kBM + q * 32 + lane;
+    uint8_t *stg = smem + L::c_off + (warp - 2) * 2 * kCBuf;
     int i = 0;
+    uint32_t nstore = 0;  // blocks this warp has stored (buffer = nstore & 1)
     for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
       const int acc = i % ACC;
       const uint32_t acc_phase = (i / ACC) & 1;
@@ -441,33 +445,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       ks_tc_fence_after();
       int tm, tn;
       tile_coords(t, num_m, num_n, group_m, tm, tn);
-      const int64_t row = int64_t(tm) * kPM + row_in_tile;
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         ks_tmem_ld32(t_addr + cc * 32, r);
         ks_tmem_wait_ld();
-        const int col0 = tn * BN + cc * 32;
-        if (row < M && num_kb > 0) {
-          uint16_t *dst = c + row * N + col0;
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            if (col0 + v * 8 < N) {
-              uint4 w;
-              w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-              w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-              w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-              w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-              *reinterpret_cast<uint4 *>(dst + v * 8) = w;
-            }
-          }
+        if (cc + 1 == BN / 32) {  // the accumulator is free for the pair's next MMAs
+          ks_tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ks_mbar_arrive_cluster(tempty_even + acc * 8);
         }
+        uint8_t *buf = stg + (nstore & 1) * kCBuf;
+        if (lane == 0) ks_bulk_wait_read<1>();  // the store two blocks back has read this buffer
+        __syncwarp();
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+          w.y = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+          w.z = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+          w.w = ks_pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+          *reinterpret_cast<uint4 *>(buf + lane * 64 + ((v ^ ((lane >> 1) & 3)) * 16)) = w;
+        }
+        ks_fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          ks_tma_store_2d(&tma_c, buf, tn * BN + cc * 32, tm * kPM + int(rank) * kBM + q * 32);
+          ks_bulk_commit_group();
+        }
+        ++nstore;
       }
-      ks_tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ks_mbar_arrive_cluster(tempty_even + acc * 8);
     }
+    if (lane == 0) ks_bulk_wait_all();  // C is in global memory before the CTA exits
   }
 
   ks_tc_fence_before();
@@ -580,6 +590,10 @@ int launch_tc2(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_
   s = ks::encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, uint64_t(a.n), uint64_t(a.k),
                          uint64_t(a.n) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != KS_OK) return s;
+  CUtensorMap tc;  // [32 columns x 32 rows] boxes, 64-byte swizzle (the epilogue's staging layout)
+  s = ks::encode_tmap_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, uint64_t(a.n), uint64_t(a.m),
+                         uint64_t(a.n) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (s != KS_OK) return s;
   auto kern = matmul_tc2_kernel<BN, STAGES, ACC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
@@ -607,8 +621,7 @@ int launch_tc2(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_
   const int64_t tiles = ((a.m + 2 * kBM - 1) / (2 * kBM)) * ((a.n + BN - 1) / BN);
   const int pairs = int(tiles < pairs_max ? tiles : pairs_max);
   lc.gridDim = dim3(2 * unsigned(pairs));
-  e = cudaLaunchKernelEx(&lc, kern, ta, tb, static_cast<uint16_t *>(a.out), int(a.m), int(a.n), int(a.k),
-                         cfg.group_m, ks::wait_ctx());
+  e = cudaLaunchKernelEx(&lc, kern, ta, tb, tc, int(a.m), int(a.n), int(a.k), cfg.group_m, ks::wait_ctx());
   if (e != cudaSuccess) return ks::map_cuda(e);
   return ks::map_cuda(cudaGetLastError());
 }
@@ -646,12 +659,11 @@ int launch_tc_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaS
 constexpr uint32_t kSmemLimit = 227 * 1024;
 
 // Per-CTA bytes: A ring + B ring (half of tile_n per CTA for the pair
-// kernel) + the C staging buffers of the one-CTA kernel's TMA-store
-// epilogue + barriers + alignment slack.
+// kernel) + the C staging buffers of the TMA-store epilogue + barriers +
+// alignment slack.
 uint32_t smem_for(int bm, int bn, int stages) {
   const uint32_t b_cols = bm == 256 ? uint32_t(bn / 2) : uint32_t(bn);
-  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + (bm == 128 ? kCStage : 0) +
-         (2 * stages + 5) * 8 + 16 + 1024;
+  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + kCStage + (2 * stages + 5) * 8 + 16 + 1024;
 }
 
 }  // namespace

@@ -918,11 +918,10 @@ ConfigVerdict validate_config(const ReductionConfig &c, const ElemProblem &p) no
 
 std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
   // per CTA: A ring (128 x 64 bf16) + B ring (64 x tile_n bf16; half of tile_n
-  // for the CTA pair of tile_m 256) + the one-CTA kernel's C staging for its
-  // TMA-store epilogue (4 warps x 2 x [32 x 32] bf16) + barriers + 1 KB
-  // alignment slack
+  // for the CTA pair of tile_m 256) + the C staging of the TMA-store epilogue
+  // (4 warps x 2 x [32 x 32] bf16) + barriers + 1 KB alignment slack
   const std::int64_t b_cols = c.tile_m == 256 ? c.tile_n / 2 : c.tile_n;
-  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * b_cols * 2) + (c.tile_m == 128 ? 16384 : 0) +
+  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * b_cols * 2) + 16384 +
          (2 * c.stages + 2 * c.acc_stages + 1) * 8 + 16 + 1024;
 }
 
