@@ -787,65 +787,78 @@ __global__ void __launch_bounds__(1024) layernorm_twopass_kernel(const uint16_t 
 // bf16 value t,
 //   x = fp32(t * fp32(1/sqrt 2)),  e = fp32(erf(double(x))),
 //   y = bf16(fp32(fp32(0.5 t) * fp32(1 + e))).
-// t has only 65536 values, so the kernels evaluate this function exactly:
-// * 2^-9 <= |t| < 8 (3072 codes): a 6 KB table of the reference's own outputs,
-//   built at kernel start from double-precision erf (the erf values lie at
-//   least 1e5 double ulps from every fp32 rounding midpoint, so any erf
-//   accurate to a few double ulps rounds to the reference's e);
-// * |t| < 2^-9: |0.5 t e| is below half a bf16 ulp of 0.5 t, so y = 0.5 t;
-// * |t| >= 8 (and inf, NaN): e rounds to +-1, so y = t for t > 0 and
-//   0.5 t * 0 (= -0, or NaN for -inf and NaN) otherwise.
-// tests/test_gelu_erf_cpu.py checks these three rules against the reference
-// for all 65536 codes; the GPU tests check the kernels bit for bit.
-constexpr uint32_t kGeluTabLo = 0x3B00u;  // bf16 bits of 2^-9
-constexpr uint32_t kGeluTabHi = 0x4100u;  // bf16 bits of 8
-constexpr int kGeluTabN = int(kGeluTabHi - kGeluTabLo);  // 1536 magnitudes
+// The kernels keep that operation order and replace the double erf by an
+// fp32 erfc of |x| with a small relative error, so that 1 + e is formed
+// from it exactly as the reference forms it:
+//   w = fp32(1 - erfc|x|)  (= fp32(erf|x|)),  1 + e = fp32(1 + w) for x >= 0
+//   and fp32(1 - w) for x < 0,
+// which also reproduces the reference's loss of the tail (for x < -3.9,
+// w rounds to 1 and y to -0).
+// erfc(z) = r * 2^((P(r) - z^2) log2 e), r = 1 / (1 + 0.55 z), z = min(|x|, 4):
+// the form of Press et al.'s erfcc (Numerical Recipes, section 6.2) with
+// this repository's own degree-6 coefficients (fit_gelu_erfc.py beside this
+// file: a least-squares fit reweighted toward minimax, relative error 3.2e-7
+// in exact arithmetic).  Over the 3072 bf16 codes with 2^-9 <= |t| < 8 the
+// result equals the reference bit for bit in a float32 emulation of this
+// operation order, even with r and the power of two off by one and two ulps
+// (rcp.approx and ex2.approx); below 2^-9, |0.5 t e| is under half a bf16 ulp
+// of 0.5 t, so y = 0.5 t (taken directly: there the erfc route would round
+// 1 - erfc coarsely); from 8 up (and inf, NaN) the clamp at z = 4 already
+// gives t or 0.5 t * 0.  tests/test_gelu_erf_cpu.py checks the emulation and
+// the closed form for all 65536 codes; the GPU tests check the kernels bit
+// for bit on all of them.
+constexpr float kErfcA = 0.55f;
+constexpr float kErfcP0 = -1.17369068f, kErfcP1 = 1.04755867f, kErfcP2 = 0.0800859705f, kErfcP3 = 0.833066046f,
+                kErfcP4 = -1.45879292f, kErfcP5 = 0.85080111f, kErfcP6 = -0.179027811f;
+constexpr uint32_t kGeluSmallBits = 0x3B00u;  // bf16 bits of 2^-9
 
-// The reference formula for bf16 bits tb (slow: one double erf).
-KS_DEV uint32_t gelu_erf_formula(uint32_t tb) {
-  const float t = __uint_as_float(tb << 16);
-  const float x = __fmul_rn(t, 0.70710678118654752f);
-  const float e = __double2float_rn(erf(double(x)));
-  return ks_f32_to_bf16(__fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.f, e)));
+KS_DEV float ks_rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// Table entries for magnitude code lo + i (i < kGeluTabN): GELU of +|t| at
-// [i], of -|t| at [kGeluTabN + i] (bf16 bits).  One erf serves both signs:
-// x(-t) = -x(t) and the rounding to fp32 is symmetric, so e(-t) = -e(t)
-// exactly.
+KS_DEV float gelu_erf(float t) {
+  const float x = __fmul_rn(t, 0.70710678118654752f);
+  const float z = fminf(fabsf(x), 4.f);
+  const float r = ks_rcp_approx(__fmaf_rn(kErfcA, z, 1.f));
+  float p = kErfcP6;
+  p = __fmaf_rn(p, r, kErfcP5);
+  p = __fmaf_rn(p, r, kErfcP4);
+  p = __fmaf_rn(p, r, kErfcP3);
+  p = __fmaf_rn(p, r, kErfcP2);
+  p = __fmaf_rn(p, r, kErfcP1);
+  p = __fmaf_rn(p, r, kErfcP0);
+  const float q = __fmul_rn(r, ks_ex2(__fmul_rn(__fmaf_rn(-z, z, p), kLog2e)));  // erfc(z)
+  const float w = __fadd_rn(1.f, -q);                                          // fp32(erf z)
+  const float s = __fadd_rn(1.f, x >= 0.f ? w : -w);                            // fp32(1 + e)
+  const float y = __fmul_rn(__fmul_rn(0.5f, t), s);
+  return (__float_as_uint(t) & 0x7fff0000u) < (kGeluSmallBits << 16) ? 0.5f * t : y;
+}
+// The same function as a table: for the 3072 codes with 2^-9 <= |t| < 8,
+// GELU of +|t| at [i] and of -|t| at [kGeluTabN + i] (bf16 bits), i = |t|'s
+// code - kGeluSmallBits; built per CTA from gelu_erf itself (3072
+// evaluations, a few microseconds per launch).  A lookup costs a few integer
+// operations and one shared-memory load, far less issue than the formula.
+constexpr uint32_t kGeluTabHi = 0x4100u;                     // bf16 bits of 8
+constexpr int kGeluTabN = int(kGeluTabHi - kGeluSmallBits);  // 1536 magnitudes
+
 KS_DEV void gelu_erf_table_entries(uint16_t *tab, int i) {
-  const float t = __uint_as_float((kGeluTabLo + uint32_t(i)) << 16);  // +|t|
-  const float x = __fmul_rn(t, 0.70710678118654752f);
-  const float e = __double2float_rn(erf(double(x)));
-  const float h = __fmul_rn(0.5f, t);
-  tab[i] = ks_f32_to_bf16(__fmul_rn(h, __fadd_rn(1.f, e)));
-  tab[kGeluTabN + i] = ks_f32_to_bf16(__fmul_rn(-h, __fadd_rn(1.f, -e)));
+  const float t = __uint_as_float((kGeluSmallBits + uint32_t(i)) << 16);  // +|t|
+  tab[i] = ks_f32_to_bf16(gelu_erf(t));
+  tab[kGeluTabN + i] = ks_f32_to_bf16(gelu_erf(-t));
 }
 
-// The codes outside the table (about 0.1 % of N(0,1) inputs), kept out of
-// line so the table lookup stays a few instructions.
-__device__ __noinline__ uint32_t gelu_erf_edge(uint32_t tb) {
-  const float t = __uint_as_float(tb << 16);
-  return ks_f32_to_bf16((tb & 0x7fffu) < kGeluTabLo ? 0.5f * t : (t > 0.f ? t : t * 0.f));
-}
-
-// GELU of the bf16 value with bits tb (low 16 bits).
-KS_DEV uint32_t gelu_erf_bits(const uint16_t *tab, uint32_t tb) {
-  const uint32_t i = (tb & 0x7fffu) - kGeluTabLo;  // wraps below the table
+// GELU of the bf16 code tb (low 16 bits) from the table; codes outside it
+// (about 0.1 % of N(0,1) inputs) are computed out of line.  The table is
+// built from gelu_erf, so both routes give the same bits.
+__device__ __noinline__ uint32_t gelu_erf_edge(uint32_t tb) { return ks_f32_to_bf16(gelu_erf(__uint_as_float(tb << 16))); }
+KS_DEV uint32_t gelu_erf_lookup(const uint16_t *tab, uint32_t tb) {
+  const uint32_t i = (tb & 0x7fffu) - kGeluSmallBits;  // wraps below the table
   if (i < uint32_t(kGeluTabN)) return tab[i + (tb >> 15) * uint32_t(kGeluTabN)];
   return gelu_erf_edge(tb);
 }
 
-// GELU of both bf16 halves of a word.
-KS_DEV uint32_t gelu_erf_pair(const uint16_t *tab, uint32_t t2) {
-  return __byte_perm(gelu_erf_bits(tab, t2 & 0xffffu), gelu_erf_bits(tab, t2 >> 16), 0x5410);
-}
-
-// Scalar form for the generic kernels (no table): the reference formula on
-// the rounded value, exact as well.
-KS_DEV float gelu_erf(float t) {
-  return ks_bf16_to_f32(uint16_t(gelu_erf_formula(ks_f32_to_bf16(t))));
-}
 KS_DEV float gelu_tanh(float t) {
   // 0.5 t (1 + tanh(u)) = t * sigmoid(2u), u = sqrt(2/pi) (t + 0.044715 t^3).
   const float u = 0.7978845608028654f * fmaf(0.044715f * t, t * t, t);
@@ -945,11 +958,15 @@ __global__ void __launch_bounds__(1024) bias_gelu_v8_kernel(const uint16_t *__re
   }
 }
 
-// Exact-erf GELU, 8-wide: each CTA first builds the 6 KB table of the
-// reference's outputs in shared memory, then walks row groups of
-// `rows_per_group` rows with a grid stride over blockIdx.y (a resident grid,
-// so the table is built once per CTA).  Each element is one shared-memory
-// lookup (rare codes outside the table take the two closed-form rules).
+// Exact-erf GELU, 8-wide.  Each CTA first builds the 6 KB table, then walks
+// row groups of `rows_per_group` rows with a grid stride over blockIdx.y (a
+// resident grid, so the table is built once per CTA; groups of 32 rows
+// measured faster than groups of 4, whose last round is better balanced).
+// Every element is one
+// shared-memory lookup: the table answers each bf16 code with the
+// reference's bits.  (Computing some pairs with gelu_erf instead, to split
+// the work between the shared-memory and the FMA/MUFU pipes, measured slower
+// at every split: 3.6-4.5 TB/s against 4.9 TB/s with the table alone.)
 template <int UNROLL>
 __global__ void __launch_bounds__(1024) bias_gelu_erf_v8_kernel(const uint16_t *__restrict__ x,
                                                                 const uint16_t *__restrict__ bias,
@@ -982,8 +999,11 @@ __global__ void __launch_bounds__(1024) bias_gelu_erf_v8_kernel(const uint16_t *
         const uint32_t in[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
         uint32_t outw[4];
 #pragma unroll
-        for (int h = 0; h < 4; ++h)  // t = bf16(x + bias): the bf16x2 add rounds the exact sum once
-          outw[h] = gelu_erf_pair(tab, as_u32(__hadd2(as_bf162(in[h]), bb[h])));
+        for (int h = 0; h < 4; ++h) {
+          // t = bf16(x + bias): the bf16x2 add rounds the exact sum once
+          const uint32_t t2 = as_u32(__hadd2(as_bf162(in[h]), bb[h]));
+          outw[h] = __byte_perm(gelu_erf_lookup(tab, t2 & 0xffffu), gelu_erf_lookup(tab, t2 >> 16), 0x5410);
+        }
         __stcs(reinterpret_cast<uint4 *>(y + (r + u) * cols + c * 8),
                make_uint4(outw[0], outw[1], outw[2], outw[3]));
       }
@@ -1410,7 +1430,8 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
   dim3 grid(unsigned((nvec + cfg.block - 1) / cfg.block), unsigned((rows + kBgRowsPerCta - 1) / kBgRowsPerCta));
   if constexpr (VEC == 8 && GELU == KS_GELU_ERF) {
     // resident grid over row groups: the table is built once per CTA
-    auto k = bias_gelu_erf_v8_kernel<4>;
+    constexpr int kUnroll = 4;
+    auto k = bias_gelu_erf_v8_kernel<kUnroll>;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, cfg.block, 0) != cudaSuccess || per_sm < 1)
       per_sm = 1;
