@@ -63,6 +63,11 @@ constexpr uint32_t kTileBytes = 2 * kBox;  // [128 x 128] tile = 32 KB
 constexpr int kStages = 2;
 
 
+// Epilogue staging: per softmax warp two [32 rows x 32 columns] bf16 blocks
+// (64-byte rows, 64-byte swizzle), 2 KB each; 8 warps = 32 KB.
+constexpr uint32_t kOBuf = 32 * 64;
+constexpr uint32_t kOStage = 8 * 2 * kOBuf;
+
 // Bytes of one [128 rows x D] bf16 tile: D / 64 boxes of 64 columns.
 template <int D>
 constexpr uint32_t tile_bytes() {
@@ -75,7 +80,8 @@ struct FaLayout {
   static constexpr uint32_t q_off = 0;                      // Q0, Q1
   static constexpr uint32_t k_off = q_off + 2 * kTB;        // K[stages]
   static constexpr uint32_t v_off = k_off + kStages * kTB;  // V[stages]
-  static constexpr uint32_t bar_off = v_off + kStages * kTB;
+  static constexpr uint32_t o_off = v_off + kStages * kTB;  // O staging for the TMA-store epilogue
+  static constexpr uint32_t bar_off = o_off + kOStage;
   // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain, p_half[2],
   // o_empty[2], q_empty
   static constexpr uint32_t n_bars = 1 + 3 * kStages + 2 + 2 + 2 + 1 + 2 + 2 + 1;
@@ -198,7 +204,7 @@ KS_DEV bool fa_item(int r, int c, int G, int num_items, int num_qb, int n_bh, in
 template <int D>
 __global__ void __launch_bounds__(kThreads2, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, uint16_t *__restrict__ out, int nq, int nk,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int nq, int nk,
                   int n_bh, float scale_log2, int causal, KsWait wait) {
   using L = FaLayout<D>;
   constexpr uint32_t kTB = L::kTB;
@@ -246,6 +252,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     ks_prefetch_tmap(&tm_q);
     ks_prefetch_tmap(&tm_k);
     ks_prefetch_tmap(&tm_v);
+    ks_prefetch_tmap(&tm_o);
   }
   if (warp == 9) {
     ks_tmem_alloc(tmem_slot, 512);
@@ -392,6 +399,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const int row = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
     const uint32_t s_col = g * 128, o_col = 256 + g * 128;
+    uint32_t nstore = 0;  // epilogue blocks stored (staging buffer = nstore & 1)
     int sg = 0;  // steps of this tile so far, over all items
     bool ok = true;
     FaItem it;
@@ -490,35 +498,48 @@ __global__ void __launch_bounds__(kThreads2, 1)
         __syncwarp();
         if (lane == 0) ks_mbar_arrive(p_full + g);
       }
-      // epilogue: O / l -> bf16 -> out[bh, qrow, :], then O is free again
+      // epilogue: O / l -> bf16, 32 columns at a time through this warp's two
+      // swizzled staging blocks, stored with TMA (rows >= nq are clipped);
+      // O is free again once its last columns are in registers
       if (!ok || !ks_mbar_wait(o_full + g, r & 1, abort, wait)) {
         ok = false;
         break;
       }
       ks_tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t *dst = out + (int64_t(it.bh) * nq + qrow) * D;
+      uint8_t *ostg = smem + L::o_off + warp * 2 * kOBuf;  // this warp's two staging blocks
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         ks_tmem_ld32(lane_addr + o_col + c * 32, o);
         ks_tmem_wait_ld();
-        if (qrow < nq) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
-            w.y = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
-            w.z = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
-            w.w = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
-            *reinterpret_cast<uint4 *>(dst + c * 32 + v * 8) = w;
-          }
+        if (c + 1 == D / 32) {
+          ks_tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ks_mbar_arrive(o_empty + g);
         }
+        uint8_t *buf = ostg + (nstore & 1) * kOBuf;
+        if (lane == 0) ks_bulk_wait_read<1>();  // the store two blocks back has read this buffer
+        __syncwarp();
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+          w.y = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+          w.z = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+          w.w = ks_pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+          *reinterpret_cast<uint4 *>(buf + lane * 64 + ((v ^ ((lane >> 1) & 3)) * 16)) = w;
+        }
+        ks_fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          ks_tma_store_3d(&tm_o, buf, c * 32, it.q0 + g * kTile + qd * 32, it.bh);
+          ks_bulk_commit_group();
+        }
+        ++nstore;
       }
-      ks_tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ks_mbar_arrive(o_empty + g);
     }
+    if (lane == 0) ks_bulk_wait_all();  // O is in global memory before the CTA exits
   }
 
   ks_tc_fence_before();
@@ -1272,12 +1293,27 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 template <int D>
 int launch_fwd(unsigned grid, cudaStream_t st, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                const ks_flash_attention_args &a, uint64_t bh, float scale_log2, int causal, bool ring) {
-  auto kern = ring ? fa_ring_kernel<D> : fa_fwd_kernel<D>;
-  const uint32_t smem = ring ? FaRingLayout<D>::smem_request : FaLayout<D>::smem_request;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e;
+  if (ring) {
+    e = cudaFuncSetAttribute(fa_ring_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(FaRingLayout<D>::smem_request));
+    if (e != cudaSuccess) return ks::map_cuda(e);
+    fa_ring_kernel<D><<<grid, kThreads2, FaRingLayout<D>::smem_request, st>>>(
+        tq, tk, tv, static_cast<uint16_t *>(a.out), int(a.nq), int(a.nk), int(bh), scale_log2, causal,
+        ks::wait_ctx());
+    return ks::map_cuda(cudaGetLastError());
+  }
+  // O: [32 columns x 32 rows] boxes per head, 64-byte swizzle (the epilogue's staging layout)
+  CUtensorMap to;
+  const uint64_t d = uint64_t(D), rs = d * 2;
+  int s = ks::encode_tmap_3d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, d, uint64_t(a.nq), bh, rs,
+                             rs * uint64_t(a.nq), 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (s != KS_OK) return s;
+  e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(FaLayout<D>::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
-  kern<<<grid, kThreads2, smem, st>>>(tq, tk, tv, static_cast<uint16_t *>(a.out), int(a.nq), int(a.nk), int(bh),
-                                      scale_log2, causal, ks::wait_ctx());
+  fa_fwd_kernel<D><<<grid, kThreads2, FaLayout<D>::smem_request, st>>>(tq, tk, tv, to, int(a.nq), int(a.nk),
+                                                                       int(bh), scale_log2, causal, ks::wait_ctx());
   return ks::map_cuda(cudaGetLastError());
 }
 

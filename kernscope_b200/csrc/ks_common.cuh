@@ -169,6 +169,12 @@ KS_DEV void ks_tma_store_2d(const CUtensorMap *m, const void *src, int c0, int c
                "r"(ks_smem_u32(src)), "r"(c0), "r"(c1)
                : "memory");
 }
+KS_DEV void ks_tma_store_3d(const CUtensorMap *m, const void *src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(ks_smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 KS_DEV void ks_bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // At most N committed bulk groups still reading their shared-memory source.
 template <int N>
