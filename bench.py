@@ -596,6 +596,11 @@ def run_families(names, args, rank, world):
                    "value": round(val, 2), "unit": unit, "ms_per_step": round(per, 5), "timing": label,
                    "roofline": {"bound": spec["bound"], "achieved": round(ach, 2), "peak": peak, "unit": unit,
                                 "frac": round(ach / peak, 4), "traffic": traffic.get(nm)}}
+        if spec["bound"] == "tensor":
+            # the timed region is steps x ms_per_step of back-to-back launches under the
+            # power cap: the sustained cuBLAS figure is the like-for-like denominator
+            out[nm]["roofline"]["peak_sustained"] = peaks["bf16_tflops_sustained"]
+            out[nm]["roofline"]["frac_sustained"] = round(ach / peaks["bf16_tflops_sustained"], 4)
         if world > 1:
             out[nm]["rank_ms_per_step"] = [round(v / steps, 5) for v in _rank_spread(my_ms, world)]
         del w
