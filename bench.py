@@ -21,7 +21,8 @@ the G GPUs (rows, elements, M-panels with B replicated, batch x head pairs),
 with efficiency t1 / (G * t_G) against the whole configuration's time on
 one GPU in the same run.  ``--scaling strong`` makes the sharded
 configuration the headline.  The reduction adds its one cross-GPU combine
-(an NCCL all-reduce of the fp64 partial) to every step.  Time = max over
+(an NCCL all-reduce of the fp64 partials, one call per eight consecutive
+jobs) to every job.  Time = max over
 ranks of CUDA-event time, barrier + synchronize on both sides, after an
 untimed pre-roll that brings the clocks back up after the barrier.
 
@@ -164,11 +165,12 @@ class Workload:
         self.ws = None
         if name == "reduction":
             self.ws = ops.reduction_workspace(self.sets[0][0][0], axis=-1, cfg=self.cfg)
-            # two fp64 partials, alternating by step, so that the cross-GPU
-            # combine of one step can overlap the next step's kernel
-            self.partials = [torch.empty(1, dtype=torch.float64, device=dev) for _ in range(2)]
+            # fp64 partials in two rows of COMBINE_BATCH steps: at N > 1 one
+            # all-reduce combines a row (the cross-GPU sums of that many
+            # consecutive jobs) while the next row's kernels run
+            self.partials = torch.empty((2, COMBINE_BATCH), dtype=torch.float64, device=dev)
 
-    def launch(self, i, stream=None):
+    def launch(self, i, stream=None, slot=None):
         ins, outs = self.sets[i % self.rotate]
         ops = self.ops
         if self.name == "softmax":
@@ -179,7 +181,7 @@ class Workload:
             ops.bias_gelu(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
         elif self.name == "reduction":
             ops.reduction(ins[0], axis=-1, out=outs[0], cfg=self.cfg, workspace=self.ws,
-                          partial_f64=self.partials[i % 2],
+                          partial_f64=self.partials.view(-1)[slot if slot is not None else 0],
                           stream=stream)
         elif self.name.startswith("matmul"):
             ops.matmul(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
@@ -270,47 +272,62 @@ def _max_over_ranks(v, world):
     return dist.max_over_ranks(v, world, device="cuda")
 
 
-def _combine(w, world, i=0):
-    """The reduction's cross-GPU combine: all-reduce of step i's fp64 partial."""
+def _combine(w, world):
+    """The reduction's cross-GPU combine of one job: all-reduce of its fp64
+    partial (slot 0, where ``launch`` writes it by default)."""
     if world > 1 and w.name == "reduction":
         from kernscope_b200 import dist
 
-        dist.combine_partials(w.partials[i % 2], world)
+        dist.combine_partials(w.partials[0, :1], world)
+
+
+# Consecutive full-sum jobs whose fp64 partials one all-reduce combines at
+# N > 1.  An all-reduce of a few bytes costs tens of microseconds of NCCL
+# latency on eight GPUs, more than one 2^25-element shard's kernel; one call
+# per COMBINE_BATCH jobs (a vector of that many partials) keeps that latency
+# behind the kernels.  Every job still gets its own cross-GPU sum.
+COMBINE_BATCH = 8
 
 
 def _reduction_steps(w, steps, world, stream, first=0):
-    """Steps first..first+steps-1 of the multi-GPU reduction with each step's
-    combine (an NCCL all-reduce of its fp64 partial) on a side stream,
-    overlapping the next step's kernel; partials alternate, so step i+2's
-    kernel waits for step i's combine.  The caller's stream waits for every
-    combine.  Used eagerly and inside a CUDA-graph capture alike."""
+    """Steps first..first+steps-1 of the multi-GPU reduction.  Step j writes
+    its fp64 partial into row (j // B) % 2, column j % B of ``w.partials``
+    (B = COMBINE_BATCH); after the last step of each row one NCCL all-reduce
+    of that row (the cross-GPU sums of its B jobs) runs on a side stream,
+    overlapping the next row's kernels, and the row is rewritten only after
+    that combine.  The caller's stream waits for every combine.  Used
+    eagerly and inside a CUDA-graph capture alike; every rank issues the same
+    collectives in the same order."""
     import torch
 
     from kernscope_b200 import dist
 
     side = getattr(w, "_side", None) or torch.cuda.Stream()
     w._side = side
-    done = []
+    B = COMBINE_BATCH
+    done = {}
     for j in range(steps):
-        i = first + j
-        if j >= 2:
-            stream.wait_event(done[j - 2])
-        w.launch(i, stream=stream)
-        k = torch.cuda.Event()
-        k.record(stream)
-        side.wait_event(k)
-        with torch.cuda.stream(side):
-            dist.combine_partials(w.partials[i % 2], world, to_f32=False)
-        c = torch.cuda.Event()
-        c.record(side)
-        done.append(c)
-    for c in done[-2:]:
-        stream.wait_event(c)
+        b, col = divmod(j, B)
+        row = b % 2
+        if col == 0 and b >= 2:
+            stream.wait_event(done[b - 2])
+        w.launch(first + j, stream=stream, slot=row * B + col)
+        if col == B - 1 or j == steps - 1:
+            k = torch.cuda.Event()
+            k.record(stream)
+            side.wait_event(k)
+            with torch.cuda.stream(side):
+                dist.combine_partials(w.partials[row, :col + 1], world, to_f32=False)
+            c = torch.cuda.Event()
+            c.record(side)
+            done[b] = c
+    for b in sorted(done)[-2:]:
+        stream.wait_event(done[b])
 
 
 def _enqueue(w, first, count, world, stream):
     """Launches first..first+count-1 (rotating buffer sets) on `stream`; the
-    multi-GPU reduction with its overlapped per-step combine."""
+    multi-GPU reduction with its overlapped, batched combines."""
     if world > 1 and w.name == "reduction":
         _reduction_steps(w, count, world, stream, first)
     else:
@@ -837,8 +854,9 @@ def main():
                        "parallelism": par,
                        "l2": "rotating input/output sets, working set >= 4x L2 (no step reads inputs from L2)",
                        "timing": f"CUDA events on the launching stream, {timing}-replayed launch loop after an "
-                                 "untimed pre-roll that follows the barrier (multi-GPU reduction: each step's "
-                                 "NCCL combine on a side stream overlapping the next step), max over ranks"},
+                                 "untimed pre-roll that follows the barrier (multi-GPU reduction: one NCCL "
+                                 "all-reduce per 8 jobs' fp64 partials on a side stream overlapping the next "
+                                 "jobs), max over ranks"},
             "roofline": {"bound": spec["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": peaks["source"]},
