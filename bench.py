@@ -79,6 +79,8 @@ WORKLOADS = {
                   "desc": "layernorm 16384x4096 bf16, gamma~N(1,0.1), beta~N(0,0.1), eps 1e-5"},
     "bias_gelu": {"config": "C3b", "shape": (16384, 16384), "bound": "hbm", "dtype": "bf16",
                   "desc": "bias_gelu (tanh) 16384x16384 bf16, bias[16384]"},
+    "bias_gelu_erf": {"config": "C3b", "shape": (16384, 16384), "bound": "hbm", "dtype": "bf16",
+                      "desc": "bias_gelu (exact erf, the reference's GELU) 16384x16384 bf16, bias[16384]"},
     "reduction": {"config": "C3c", "shape": (1 << 28,), "bound": "hbm", "dtype": "f32",
                   "desc": "full fp32 sum of 2^28 uniform[0,1) (fp64 partials, NCCL combine for N>1)"},
     "matmul": {"config": "C4", "shape": (8192, 8192, 8192), "bound": "tensor", "dtype": "bf16",
@@ -88,6 +90,10 @@ WORKLOADS = {
     "flash_attention": {"config": "C5", "shape": (8, 32, 8192, 128), "bound": "tensor", "dtype": "bf16",
                         "desc": "flash attention fwd causal B8 H32 N8192 d128 bf16"},
 }
+
+
+# the row-wise families: rows shard, and the end-to-end leg pipelines row chunks
+ROW_FAMILIES = ("softmax", "layernorm", "bias_gelu", "bias_gelu_erf")
 
 
 class Workload:
@@ -122,14 +128,15 @@ class Workload:
             self.make = lambda: [torch.randn((r, c), generator=g, device=dev).to(torch.bfloat16), gamma, beta]
             self.outs = lambda: [torch.empty((r, c), dtype=torch.bfloat16, device=dev)]
             self.cfg = ops.default_layernorm_config(c)
-        elif name == "bias_gelu":
+        elif name in ("bias_gelu", "bias_gelu_erf"):
             r, c = shape
+            self.gelu = "erf" if name == "bias_gelu_erf" else "tanh"
             self.in_bytes, self.out_bytes = r * c * 2 + c * 2, r * c * 2
             self.alg_bytes, self.flops = r * c * 4 + c * 2, 0
             bias = (0.1 * torch.randn(c, generator=g, device=dev)).to(torch.bfloat16)
             self.make = lambda: [torch.randn((r, c), generator=g, device=dev).to(torch.bfloat16), bias]
             self.outs = lambda: [torch.empty((r, c), dtype=torch.bfloat16, device=dev)]
-            self.cfg = ops.default_bias_gelu_config(c, "tanh")
+            self.cfg = ops.default_bias_gelu_config(c, self.gelu)
             self.extra["reference_model_bytes"] = r * c * 2 * 3
         elif name == "reduction":
             (n,) = shape
@@ -177,8 +184,8 @@ class Workload:
             ops.softmax(ins[0], out=outs[0], cfg=self.cfg, stream=stream)
         elif self.name == "layernorm":
             ops.layernorm(ins[0], ins[1], ins[2], out=outs[0], cfg=self.cfg, stream=stream)
-        elif self.name == "bias_gelu":
-            ops.bias_gelu(ins[0], ins[1], out=outs[0], cfg=self.cfg, stream=stream)
+        elif self.name.startswith("bias_gelu"):
+            ops.bias_gelu(ins[0], ins[1], gelu=self.gelu, out=outs[0], cfg=self.cfg, stream=stream)
         elif self.name == "reduction":
             ops.reduction(ins[0], axis=-1, out=outs[0], cfg=self.cfg, workspace=self.ws,
                           partial_f64=self.partials.view(-1)[slot if slot is not None else 0],
@@ -190,7 +197,8 @@ class Workload:
 
     def config_name(self):
         return self.N.kernel_symbol("flash_attention" if self.name == "flash_attention" else
-                                    "matmul" if self.name.startswith("matmul") else self.name, self.cfg)
+                                    "matmul" if self.name.startswith("matmul") else
+                                    "bias_gelu" if self.name.startswith("bias_gelu") else self.name, self.cfg)
 
 
 # ---------------------------------------------------------------------------
@@ -425,7 +433,7 @@ def measure_e2e(w, steps, world):
     h2d = sum(t.numel() * t.element_size() for t in ins)
     d2h = outs[0].numel() * outs[0].element_size()
 
-    if w.name in ("softmax", "layernorm", "bias_gelu"):
+    if w.name in ROW_FAMILIES:
         rows = ins[0].shape[0]
         pipe = ops.HostRowPipeline(rows)
         row_in = [0]  # x is row-sharded; gamma/beta/bias stay whole
@@ -438,7 +446,7 @@ def measure_e2e(w, steps, world):
             elif w.name == "layernorm":
                 ops.layernorm(x, ins[1], ins[2], out=y, cfg=w.cfg, stream=st)
             else:
-                ops.bias_gelu(x, ins[1], out=y, cfg=w.cfg, stream=st)
+                ops.bias_gelu(x, ins[1], gelu=w.gelu, out=y, cfg=w.cfg, stream=st)
 
         def step():
             if h2d_whole and pipe.ev_k[-1] is not None:
@@ -466,7 +474,7 @@ def measure_e2e(w, steps, world):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(world)
     e0.record(stream)
-    if w.name in ("softmax", "layernorm", "bias_gelu"):
+    if w.name in ROW_FAMILIES:
         pipe.s_in.wait_stream(stream)  # the copies start after the start event
     for _ in range(steps):
         step()
@@ -503,10 +511,11 @@ def cpu_baseline(name, shape, budget_s=10.0):
             d = oin.baseline_inputs("layernorm", shape, seed=2, row0=0, nrows=min(rows, r))
             t0 = time.perf_counter(); orf.layernorm(d["x"], d["gamma"], d["beta"]); dt = time.perf_counter() - t0
             u = d["x"].shape[0] * c * 4 / 1e9; sample = f"{d['x'].shape[0]} of {r} rows"
-        elif name == "bias_gelu":
+        elif name.startswith("bias_gelu"):
             r, c = shape
             d = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=0, nrows=min(rows, r))
-            t0 = time.perf_counter(); orf.bias_gelu_tanh(d["x"], d["bias"]); dt = time.perf_counter() - t0
+            fn = orf.bias_gelu if name == "bias_gelu_erf" else orf.bias_gelu_tanh
+            t0 = time.perf_counter(); fn(d["x"], d["bias"]); dt = time.perf_counter() - t0
             u = d["x"].shape[0] * c * 4 / 1e9; sample = f"{d['x'].shape[0]} of {r} rows"
         elif name == "reduction":
             (n,) = shape
@@ -571,7 +580,7 @@ def _job_units(nm, shape, bound):
     elif nm == "layernorm":
         r, c = shape
         b = r * c * 4 + 2 * c * 2
-    elif nm == "bias_gelu":
+    elif nm.startswith("bias_gelu"):
         r, c = shape
         b = r * c * 4 + c * 2
     elif nm == "reduction":
@@ -640,7 +649,7 @@ def _ref_worker_init():
 
 # Rows (matmul: A rows; attention: query rows; reduction: 64K-element blocks)
 # per worker per step, sized to ~0.1-0.5 s of numpy work on one core.
-REF_CHUNK = {"softmax": 256, "layernorm": 512, "bias_gelu": 64, "reduction": 512, "matmul": 256,
+REF_CHUNK = {"softmax": 256, "layernorm": 512, "bias_gelu": 64, "bias_gelu_erf": 64, "reduction": 512, "matmul": 256,
              "matmul_65536": 256, "flash_attention": 256}
 
 
@@ -725,7 +734,7 @@ def _ref_chunk(job):
     from oracle import refs as orf
 
     shape = WORKLOADS[name]["shape"]
-    if name in ("softmax", "layernorm", "bias_gelu"):
+    if name in ROW_FAMILIES:
         rows = shape[0]
         row0 %= rows
         nrows = min(nrows, rows - row0)
@@ -737,9 +746,10 @@ def _ref_chunk(job):
         d = oin.baseline_inputs("layernorm", shape, seed=2, row0=row0, nrows=nrows)
         t0 = time.perf_counter(); orf.layernorm(d["x"], d["gamma"], d["beta"]); dt = time.perf_counter() - t0
         return d["x"].size * 4 / 1e9, dt
-    if name == "bias_gelu":
+    if name.startswith("bias_gelu"):
         d = oin.baseline_inputs("bias_gelu", shape, seed=2, row0=row0, nrows=nrows)
-        t0 = time.perf_counter(); orf.bias_gelu_tanh(d["x"], d["bias"]); dt = time.perf_counter() - t0
+        fn = orf.bias_gelu if name == "bias_gelu_erf" else orf.bias_gelu_tanh
+        t0 = time.perf_counter(); fn(d["x"], d["bias"]); dt = time.perf_counter() - t0
         return d["x"].size * 4 / 1e9, dt
     if name == "reduction":
         (n,) = shape
@@ -828,7 +838,8 @@ def main():
     if not args.no_families:
         # the heaviest (power-capped) workload last, so it does not heat the GPU
         # for the others
-        order = ["layernorm", "bias_gelu", "reduction", "softmax", "flash_attention", "matmul", "matmul_65536"]
+        order = ["layernorm", "bias_gelu", "bias_gelu_erf", "reduction", "softmax", "flash_attention", "matmul",
+                 "matmul_65536"]
         names = [n for n in order if n != args.workload]
         fams = run_families(names, args, rank, world)
     cpu = None

@@ -958,7 +958,9 @@ __global__ void __launch_bounds__(1024) bias_gelu_v8_kernel(const uint16_t *__re
   }
 }
 
-// Exact-erf GELU, 8-wide.  Each CTA first builds the 6 KB table, then walks
+// Exact-erf GELU, 8-wide, for CTAs below 1024 threads (1024-thread CTAs use
+// the whole-code table, bias_gelu_erf_codes_kernel).  Each CTA first builds
+// the 6 KB table, then walks
 // row groups of `rows_per_group` rows with a grid stride over blockIdx.y (a
 // resident grid, so the table is built once per CTA; groups of 32 rows
 // measured faster than groups of 4, whose last round is better balanced).
@@ -1006,6 +1008,80 @@ __global__ void __launch_bounds__(1024) bias_gelu_erf_v8_kernel(const uint16_t *
         }
         __stcs(reinterpret_cast<uint4 *>(y + (r + u) * cols + c * 8),
                make_uint4(outw[0], outw[1], outw[2], outw[3]));
+      }
+    }
+  }
+}
+
+// Exact-erf GELU of every bf16 code, for the whole-code table below.  Codes
+// take one of three routes, each giving the bits gelu_erf gives:
+//   * |t| < 2^-9 (zeros and subnormals included): bf16(0.5 t), gelu_erf's
+//     own small-input branch;
+//   * 8 <= |t| < inf: erfc(min(|x|, 4)) is below 2^-25, so w = fp32(1 - erfc)
+//     rounds to 1 and 1 + e is 2 (t >= 8) or 0 (t <= -8): y = t, or -0;
+//   * everything else (2^-9 <= |t| < 8, the infinities and NaN): gelu_erf.
+KS_DEV uint32_t gelu_erf_code(uint32_t code) {
+  const uint32_t e = code & 0x7fffu;
+  if (e < kGeluSmallBits) return ks_f32_to_bf16(0.5f * __uint_as_float(code << 16));
+  if (e >= kGeluTabHi && e < 0x7f80u) return (code & 0x8000u) ? 0x8000u : code;
+  return ks_f32_to_bf16(gelu_erf(__uint_as_float(code << 16)));
+}
+constexpr int kGeluCodeWords = 1 << 15;                            // two codes per 32-bit word
+constexpr size_t kGeluCodeTableBytes = size_t(kGeluCodeWords) * 4;  // 128 KB
+
+// Exact-erf GELU, 8-wide, from a table of all 65536 codes: an element costs
+// a 16-bit extract and one shared-memory load, with no range test and no
+// sign handling (the 3072-entry table above needs both, and the kernel that
+// uses it is issue-bound at 75 % of the copy bandwidth).  The table takes
+// 128 KB, so a CTA of 1024 threads owns an SM; it builds the table (3328
+// formula evaluations, the rest closed forms) after issuing its first rows'
+// loads, then walks row groups with a grid stride over blockIdx.y.
+template <int UNROLL>
+__global__ void __launch_bounds__(1024) bias_gelu_erf_codes_kernel(const uint16_t *__restrict__ x,
+                                                                   const uint16_t *__restrict__ bias,
+                                                                   uint16_t *__restrict__ y, int64_t total,
+                                                                   int64_t cols, int64_t rows, int rows_per_group) {
+  extern __shared__ uint32_t gelu_code_words[];  // word k: code 2k (low half), code 2k+1 (high half)
+  const uint16_t *tab = reinterpret_cast<const uint16_t *>(gelu_code_words);
+  const int64_t nvec = cols / 8;
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t groups = (rows + rows_per_group - 1) / rows_per_group;
+  auto load = [&](int64_t g, int64_t r, uint4 *w) {
+    const int64_t r1 = min(rows, (g + 1) * rows_per_group);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t off = (r + u) * cols + c * 8;
+      if (r + u < r1 && off + 8 <= total) w[u] = __ldcs(reinterpret_cast<const uint4 *>(x + off));
+    }
+  };
+  uint4 w[UNROLL];
+  int64_t g = blockIdx.y;
+  if (c < nvec && g < groups) load(g, g * rows_per_group, w);
+  for (int k = threadIdx.x; k < kGeluCodeWords; k += blockDim.x)
+    gelu_code_words[k] = gelu_erf_code(2u * k) | (gelu_erf_code(2u * k + 1) << 16);
+  __syncthreads();
+  if (c >= nvec) return;
+  const uint4 bw = __ldg(reinterpret_cast<const uint4 *>(bias) + c);
+  const __nv_bfloat162 bb[4] = {as_bf162(bw.x), as_bf162(bw.y), as_bf162(bw.z), as_bf162(bw.w)};
+  bool loaded = true;
+  for (; g < groups; g += gridDim.y) {
+    const int64_t r1 = min(rows, (g + 1) * rows_per_group);
+    for (int64_t r = g * rows_per_group; r < r1; r += UNROLL) {
+      if (!loaded) load(g, r, w);
+      loaded = false;
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int64_t off = (r + u) * cols + c * 8;
+        if (!(r + u < r1 && off + 8 <= total)) continue;
+        const uint32_t in[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+        uint32_t outw[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          // t = bf16(x + bias): the bf16x2 add rounds the exact sum once
+          const uint32_t t2 = as_u32(__hadd2(as_bf162(in[h]), bb[h]));
+          outw[h] = __byte_perm(tab[t2 & 0xffffu], tab[t2 >> 16], 0x5410);
+        }
+        __stcs(reinterpret_cast<uint4 *>(y + off), make_uint4(outw[0], outw[1], outw[2], outw[3]));
       }
     }
   }
@@ -1420,6 +1496,22 @@ constexpr int kBgRowsPerCta = 32;
 template <int VEC>
 constexpr int bg_unroll() { return VEC == 8 ? 2 : 4; }
 
+// The vector kernels stop at the last full VEC chunk of a ragged last row;
+// the scalar tail kernel finishes it.
+template <int VEC, int GELU>
+int launch_bias_gelu_tail(const ks_bias_gelu_args &a, int64_t rows, cudaStream_t st) {
+  const int64_t last_row_start = (rows - 1) * a.cols;
+  const int64_t tail_len = a.total - last_row_start;
+  const int64_t vec_done = (tail_len / VEC) * VEC;
+  if (vec_done >= tail_len) return KS_OK;
+  const int64_t start = last_row_start + vec_done;
+  const int64_t n = a.total - start;
+  bias_gelu_tail_kernel<GELU><<<unsigned((n + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint16_t *>(a.x), static_cast<const uint16_t *>(a.bias), static_cast<uint16_t *>(a.out),
+      start, a.total, a.cols);
+  return ks::map_cuda(cudaGetLastError());
+}
+
 template <int VEC, int GELU>
 int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args &a, cudaStream_t st) {
   auto x = static_cast<const uint16_t *>(a.x);
@@ -1429,7 +1521,24 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
   const int64_t nvec = a.cols / VEC;
   dim3 grid(unsigned((nvec + cfg.block - 1) / cfg.block), unsigned((rows + kBgRowsPerCta - 1) / kBgRowsPerCta));
   if constexpr (VEC == 8 && GELU == KS_GELU_ERF) {
-    // resident grid over row groups: the table is built once per CTA
+    if (cfg.block == 1024) {
+      // one CTA per SM with the 128 KB table of every code, resident grid over row groups
+      auto k = bias_gelu_erf_codes_kernel<4>;
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGeluCodeTableBytes));
+      if (e != cudaSuccess) return ks::map_cuda(e);
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 1024, kGeluCodeTableBytes) != cudaSuccess ||
+          per_sm < 1)
+        per_sm = 1;
+      const int64_t resident = int64_t(per_sm) * ks::sm_count();
+      const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(grid.y, resident / std::max<int64_t>(1, grid.x)));
+      k<<<dim3(grid.x, unsigned(gy)), 1024, kGeluCodeTableBytes, st>>>(x, b, y, a.total, a.cols, rows,
+                                                                      kBgRowsPerCta);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return ks::map_cuda(e);
+      return launch_bias_gelu_tail<VEC, GELU>(a, rows, st);
+    }
+    // resident grid over row groups: the 6 KB table is built once per CTA
     constexpr int kUnroll = 4;
     auto k = bias_gelu_erf_v8_kernel<kUnroll>;
     int per_sm = 0;
@@ -1445,17 +1554,7 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
                                                                               kBgRowsPerCta);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ks::map_cuda(e);
-  // The vector kernel stops at the last full VEC chunk of a ragged last row.
-  const int64_t last_row_start = (rows - 1) * a.cols;
-  const int64_t tail_len = a.total - last_row_start;
-  const int64_t vec_done = (tail_len / VEC) * VEC;
-  if (vec_done < tail_len) {
-    const int64_t start = last_row_start + vec_done;
-    const int64_t n = a.total - start;
-    bias_gelu_tail_kernel<GELU><<<unsigned((n + 255) / 256), 256, 0, st>>>(x, b, y, start, a.total, a.cols);
-    e = cudaGetLastError();
-  }
-  return ks::map_cuda(e);
+  return launch_bias_gelu_tail<VEC, GELU>(a, rows, st);
 }
 
 }  // namespace

@@ -85,7 +85,7 @@ def strong_shard(family: str, shape, rank: int, world: int):
     families, elements of the full sum, M-panels of the GEMM (B replicated),
     batch x head pairs of attention.  Returns (shard shape, description)."""
     shape = tuple(int(v) for v in shape)
-    if family in ("softmax", "layernorm", "bias_gelu"):
+    if family in ("softmax", "layernorm", "bias_gelu", "bias_gelu_erf"):
         r0, r1 = shard_rows(shape[0], rank, world)
         return (r1 - r0, shape[1]), f"rows [{r0}, {r1}) of {shape[0]}"
     if family == "reduction":

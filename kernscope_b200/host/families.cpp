@@ -723,7 +723,12 @@ class RowFamily : public Family {
       // axis 0 stages every thread's column partials (block x vec_width fp32)
       if (axis_of(s) == 0) res.smem_bytes = block * iget(cfg, "vec_width", 8) * 4 + 16;
     }
-    if (kind == RowKind::kBiasGelu) res.regs_per_thread = 61;
+    if (kind == RowKind::kBiasGelu) {
+      res.regs_per_thread = 61;
+      // 8-wide erf: a 128 KB table of every bf16 code at 1024 threads, a
+      // 6 KB table of the 3072 non-trivial codes below
+      if (gelu == KS_GELU_ERF && iget(cfg, "vec_width", 8) == 8) res.smem_bytes = block == 1024 ? 131072 : 6144;
+    }
     if (mode == KS_MODE_CLUSTER) {
       res.regs_per_thread = 50;  // up to four 8-wide chunks per thread
       res.smem_bytes = 288;      // warp partials and the cluster slots

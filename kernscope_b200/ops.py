@@ -79,7 +79,11 @@ def default_layernorm_config(cols: int, rows: int | None = None) -> N.LayerNormC
 
 def default_bias_gelu_config(cols: int, gelu: str = "tanh") -> N.BiasGeluConfig:
     vec = 8 if cols % 8 == 0 else 4 if cols % 4 == 0 else 2 if cols % 2 == 0 else 1
-    return N.BiasGeluConfig(128, vec, N.KS_GELU_TANH if gelu == "tanh" else N.KS_GELU_ERF)
+    if gelu != "tanh":
+        # 8-wide erf: 1024 threads run the kernel that looks every bf16 code up
+        # in a shared-memory table (one CTA per SM)
+        return N.BiasGeluConfig(1024 if vec == 8 else 128, vec, N.KS_GELU_ERF)
+    return N.BiasGeluConfig(128, vec, N.KS_GELU_TANH)
 
 
 def default_reduction_config(cols: int, axis: int) -> N.ReductionConfig:

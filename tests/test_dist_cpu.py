@@ -94,8 +94,8 @@ def test_failed_rank_ends_collective_with_error():
     assert errs[0] is not None  # the surviving rank's all-reduce errored out instead of hanging
 
 
-@pytest.mark.parametrize("family", ["softmax", "layernorm", "bias_gelu", "reduction", "matmul", "matmul_65536",
-                                    "flash_attention"])
+@pytest.mark.parametrize("family", ["softmax", "layernorm", "bias_gelu", "bias_gelu_erf", "reduction", "matmul",
+                                    "matmul_65536", "flash_attention"])
 def test_strong_shards_partition_the_job(family):
     """Strong scaling: the G shards of a benchmark configuration cover the
     whole job exactly (rows, elements, M-panels, batch x head pairs), so the
@@ -112,7 +112,7 @@ def test_strong_shards_partition_the_job(family):
     for world in (1, 2, 4, 8):
         shards = [dist.strong_shard(family, wl["shape"], r, world)[0] for r in range(world)]
         parts = [bench._job_units(family, sh, wl["bound"]) for sh in shards]
-        if family in ("layernorm", "bias_gelu"):  # gamma/beta/bias are read by every shard
+        if family in ("layernorm", "bias_gelu", "bias_gelu_erf"):  # gamma/beta/bias are read by every shard
             extra = (world - 1) * (2 * wl["shape"][1] * 2 if family == "layernorm" else wl["shape"][1] * 2) / 1e9
             assert abs(sum(parts) - extra - full) <= 1e-9 * full
         elif family == "reduction":  # every shard writes its own 4-byte result

@@ -88,3 +88,35 @@ def test_small_inputs_take_half_t():
         ref = orf.gelu_erf(t[small]).view(np.uint16)
     y = (np.float32(0.5) * t[small].astype(np.float32)).astype(ml_dtypes.bfloat16).view(np.uint16)
     assert np.array_equal(y, ref)
+
+
+def test_large_inputs_closed_form():
+    """From |t| = 8 up to the largest finite bf16, erf(x) rounds to 1 in fp32:
+    the reference returns t for t > 0 and -0 for t < 0, the closed form the
+    whole-code table (rowops.cu, gelu_erf_code) stores for those codes."""
+    bits, t = _codes()
+    mag = bits & 0x7FFF
+    big = (mag >= 0x4100) & (mag < 0x7F80)
+    ref = orf.gelu_erf(t[big]).view(np.uint16)
+    want = np.where(bits[big] & 0x8000, np.uint16(0x8000), bits[big])
+    assert np.array_equal(ref, want)
+
+
+def test_code_table_routes_cover_every_code():
+    """The table's three routes (0.5 t below 2^-9, the closed form from 8 up,
+    the formula between and for inf/NaN) equal the reference on every code."""
+    fit = _fit_module()
+    a, c = _kernel_coefficients()
+    bits, t = _codes()
+    tf = t.astype(np.float32)
+    mag = bits & 0x7FFF
+    with np.errstate(invalid="ignore", over="ignore"):
+        formula = fit.gelu_emulated(tf, c, a=a).astype(ml_dtypes.bfloat16).view(np.uint16)
+        half = (np.float32(0.5) * tf).astype(ml_dtypes.bfloat16).view(np.uint16)
+        ref = orf.gelu_erf(t).view(np.uint16)
+    closed = np.where(bits & 0x8000, np.uint16(0x8000), bits)
+    table = np.where(mag < SMALL, half, np.where((mag >= 0x4100) & (mag < 0x7F80), closed, formula))
+    fref = ref.view(ml_dtypes.bfloat16).astype(np.float32)
+    ftab = table.view(ml_dtypes.bfloat16).astype(np.float32)
+    same = (table == ref) | (np.isnan(fref) & np.isnan(ftab))
+    assert same.all(), [hex(int(b)) for b in bits[~same][:8]]

@@ -252,6 +252,19 @@ def test_bias_gelu_erf_bit_exact_baseline_rows(ks):
     assert _same_bf16_bits(y, orf.bias_gelu(inp["x"], inp["bias"])).all()
 
 
+@pytest.mark.parametrize("shape", [(1000, 16384), (77, 8200), (3, 8), (2, 1 << 21)])
+def test_bias_gelu_erf_code_table_shapes(ks, shape):
+    """The 1024-thread 8-wide erf kernel (a shared-memory table of every bf16
+    code, resident grid over 32-row groups) is bit-identical to the oracle
+    with a ragged last row group, a last column CTA with one active thread,
+    a single row group, and more column CTAs than SMs."""
+    N, ops = ks
+    inp = oin.generate_inputs("bias_gelu", shape, seed=21)
+    cfg = N.BiasGeluConfig(1024, 8, N.KS_GELU_ERF)
+    y = to_numpy(ops.bias_gelu(to_torch(inp["x"]), to_torch(inp["bias"]), gelu="erf", cfg=cfg))
+    assert _same_bf16_bits(y, orf.bias_gelu(inp["x"], inp["bias"])).all()
+
+
 @pytest.mark.parametrize("gelu", ["erf", "tanh"])
 def test_bias_gelu_baseline_sampled(ks, gelu):
     _, ops = ks
@@ -277,14 +290,15 @@ def test_bias_gelu_ragged_total(ks):
     out = torch.empty_like(x)
     import ctypes as C
 
-    for vec in (1, 2, 4, 8):
-        cfg = N.BiasGeluConfig(128, vec, N.KS_GELU_ERF)
+    idx = np.arange(total)
+    exp = orf.gelu_erf(orf.to_bf16(xflat.astype(np.float32) + inp["bias"][idx % cols].astype(np.float32)))
+    for block, vec in itertools.product((128, 1024), (1, 2, 4, 8)):
+        cfg = N.BiasGeluConfig(block, vec, N.KS_GELU_ERF)
         args = N.BiasGeluArgs(x.data_ptr(), b.data_ptr(), out.data_ptr(), total, cols)
+        out.zero_()
         N.check("launch", N.lib.ks_bias_gelu_launch(C.byref(cfg), C.byref(args), None))
         torch.cuda.synchronize()
-        idx = np.arange(total)
-        exp = orf.gelu_erf(orf.to_bf16(xflat.astype(np.float32) + inp["bias"][idx % cols].astype(np.float32)))
-        assert_bf16_close(to_numpy(out), exp)
+        assert _same_bf16_bits(to_numpy(out), exp).all(), (block, vec)
 
 
 @pytest.mark.parametrize("rows,chunk", [(4096, 512), (1000, 333), (7, 64)])
