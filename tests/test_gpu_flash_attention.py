@@ -126,6 +126,32 @@ def test_attention_large_logits(ks, tiles):
     _check_mh(o, q, k, v, True)
 
 
+@pytest.mark.parametrize("tiles", TILES, ids=lambda t: f"m{t[0]}n{t[1]}")
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("d", [128, 64])
+def test_attention_score_jumps(ks, tiles, causal, d):
+    """Scores that jump far above every earlier key of their row: inside a
+    128-key tile (key 100, about 2^76 above keys 0-63 in exp2 terms), a
+    moderate rise in the next tile (key 200, about 2^13 higher) and another
+    far jump in the first half of a later tile (key 300, about 2^100
+    higher).  The kernels move their exponent offset and rescale the P and O
+    they already hold; a missed rescale leaves earlier terms 2^64 or more
+    too large."""
+    N, ops = ks
+    b, h, n = 1, 2, 512
+    g = np.random.default_rng(31)
+    q, k, v = (g.standard_normal((b, h, n, d), dtype=np.float32) for _ in range(3))
+    q[..., 0] = 10.0  # a component every query shares
+    k[..., 100, 0] = 60.0
+    k[..., 200, 0] = 70.0
+    k[..., 300, 0] = 150.0
+    q, k, v = (orf.to_bf16(x) for x in (q, k, v))
+    cfg = N.FlashAttentionConfig(tiles[0], tiles[1], 2, int(causal))
+    o = to_numpy(ops.flash_attention(to_torch(q), to_torch(k), to_torch(v), causal=causal, cfg=cfg))
+    assert np.isfinite(o.astype(np.float32)).all()
+    _check_mh(o, q, k, v, causal)
+
+
 @pytest.mark.parametrize("tile_n", [128, 64])
 def test_attention_c5_sampled(ks, tile_n):
     """C5: B8 H32 N8192 d128 causal, Q/K/V ~ N(0,1); heads (0,0) and (7,31)
