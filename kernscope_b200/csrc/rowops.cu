@@ -1496,6 +1496,16 @@ constexpr int kBgRowsPerCta = 32;
 template <int VEC>
 constexpr int bg_unroll() { return VEC == 8 ? 2 : 4; }
 
+// Rows per group for a resident grid of gy row-group slots: about
+// kBgRowsPerCta, sized so that every slot walks the same number of groups
+// (8192 rows on 74 slots: 4 groups of 28 rows each, where groups of 32 would
+// leave the fourth round a third full), a multiple of the kernels' 4-row step.
+inline int balanced_rows_per_group(int64_t rows, int64_t gy) {
+  const int64_t rounds = std::max<int64_t>(1, (rows + gy * kBgRowsPerCta - 1) / (gy * kBgRowsPerCta));
+  const int64_t rpg = (rows + gy * rounds - 1) / (gy * rounds);
+  return int(std::max<int64_t>(4, (rpg + 3) / 4 * 4));
+}
+
 // The vector kernels stop at the last full VEC chunk of a ragged last row;
 // the scalar tail kernel finishes it.
 template <int VEC, int GELU>
@@ -1533,7 +1543,7 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
       const int64_t resident = int64_t(per_sm) * ks::sm_count();
       const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(grid.y, resident / std::max<int64_t>(1, grid.x)));
       k<<<dim3(grid.x, unsigned(gy)), 1024, kGeluCodeTableBytes, st>>>(x, b, y, a.total, a.cols, rows,
-                                                                      kBgRowsPerCta);
+                                                                      balanced_rows_per_group(rows, gy));
       e = cudaGetLastError();
       if (e != cudaSuccess) return ks::map_cuda(e);
       return launch_bias_gelu_tail<VEC, GELU>(a, rows, st);
@@ -1546,7 +1556,8 @@ int launch_bias_gelu_vec(const ks_bias_gelu_config &cfg, const ks_bias_gelu_args
       per_sm = 1;
     const int64_t resident = int64_t(per_sm) * ks::sm_count();
     const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(grid.y, resident / std::max<int64_t>(1, grid.x)));
-    k<<<dim3(grid.x, unsigned(gy)), cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
+    k<<<dim3(grid.x, unsigned(gy)), cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows,
+                                                        balanced_rows_per_group(rows, gy));
   } else if constexpr (VEC == 8)
     bias_gelu_v8_kernel<GELU, 4><<<grid, cfg.block, 0, st>>>(x, b, y, a.total, a.cols, rows, kBgRowsPerCta);
   else
