@@ -683,7 +683,10 @@ class RowFamily : public Family {
 
   std::vector<json> enumerate(bool full, const std::vector<std::int64_t> &s) const override {
     std::vector<json> v;
-    const std::vector<int> blocks = full ? std::vector<int>{128, 256, 512, 1024} : std::vector<int>{128, 256, 512};
+    // bias_gelu keeps 1024 in the bounded grid: its 8-wide erf kernel at
+    // 1024 threads (a table of every bf16 code, one CTA per SM) is the fastest
+    const std::vector<int> blocks = full || kind == RowKind::kBiasGelu ? std::vector<int>{128, 256, 512, 1024}
+                                                                       : std::vector<int>{128, 256, 512};
     const std::vector<int> vecs = full ? std::vector<int>{1, 2, 4, 8} : std::vector<int>{4, 8};
     std::vector<std::string> modes;
     if (kind == RowKind::kSoftmax || kind == RowKind::kLayerNorm) modes = {"onepass", "twopass", "staged", "cluster"};
