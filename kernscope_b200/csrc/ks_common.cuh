@@ -159,6 +159,30 @@ KS_DEV void ks_tma_load_3d(void *dst, const CUtensorMap *m, uint64_t *bar, int c
       : "memory");
 }
 
+// L2 eviction priority for the cache-hinted loads below: lines loaded with
+// this policy are evicted after normal ones.
+KS_DEV uint64_t ks_l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// The tiled loads above with an L2 cache policy.
+KS_DEV void ks_tma_load_2d_hint(void *dst, const CUtensorMap *m, uint64_t *bar, int c0, int c1, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(ks_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(ks_smem_u32(bar)), "r"(c0), "r"(c1), "l"(pol)
+      : "memory");
+}
+KS_DEV void ks_tma_load_3d_hint(void *dst, const CUtensorMap *m, uint64_t *bar, int c0, int c1, int c2,
+                                uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(ks_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(ks_smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
+      : "memory");
+}
+
 // TMA store of a 2-D box from this CTA's shared memory (bulk-group
 // completion: commit, then wait_group.read before the buffer is rewritten and
 // wait_group 0 before exit).  Non-negative coordinates only; the innermost

@@ -4,7 +4,8 @@
 // tiles in shared memory and accumulates with scalar FMAs.  Here:
 //
 //   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256),
-//     raster grouped by `group_m` M-tiles for L2 reuse;
+//     raster grouped by `group_m` M-tiles for L2 reuse (or, group_m < 0,
+//     banded by N-tiles with the band's B panels kept in L2);
 //   * warp 0 (one lane) is the TMA producer: per K-block of 64 it loads the
 //     A box [128 rows x 64 K] and BN/64 B boxes [64 K x 64 N], all with the
 //     128-byte swizzle, into a STAGES-deep shared-memory ring (full/empty
@@ -57,7 +58,23 @@ struct MmLayout {
                                         : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
 };
 
+// Output tile t of the persistent raster.  group_m > 0: groups of group_m
+// M-tiles, M-tiles fastest, so the A panels of a group are reused while B
+// streams past.  group_m < 0: bands of -group_m N-tiles, N-tiles fastest, so
+// the band's B panels (loaded with evict_last) stay in L2 while all of A
+// streams past once per band; for tall problems (M >> N) this reads less.
 KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &tn) {
+  if (group_m < 0) {
+    const int band_n = -group_m;
+    const int band_size = band_n * num_m;
+    const int b = t / band_size;
+    const int first_n = b * band_n;
+    const int bn = min(num_n - first_n, band_n);
+    const int r = t - b * band_size;
+    tn = first_n + r % bn;
+    tm = r / bn;
+    return;
+  }
   const int group_size = group_m * num_n;
   const int g = t / group_size;
   const int first_m = g * group_m;
@@ -121,6 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t armed = 0, armed_parity = 0;  // per-stage bits for the teardown wait
     bool ok = true;
+    const bool keep_b = group_m < 0;  // N-band raster: the band's B panels stay in L2
+    const uint64_t pol = ks_l2_policy_evict_last();
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, num_m, num_n, group_m, tm, tn);
@@ -135,11 +154,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
         if (b3d) {
           // one copy for all BN/64 column blocks (tensor map dims: 64 columns, K, N/64)
-          ks_tma_load_3d(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64));
+          if (keep_b)
+            ks_tma_load_3d_hint(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64), pol);
+          else
+            ks_tma_load_3d(b_dst, &tma_b, full + stage, 0, kb * kBK, tn * (BN / 64));
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+          for (int j = 0; j < BN / 64; ++j) {
+            if (keep_b)
+              ks_tma_load_2d_hint(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK, pol);
+            else
+              ks_tma_load_2d(b_dst + j * kBBoxBytes, &tma_b, full + stage, tn * BN + j * 64, kb * kBK);
+          }
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -698,8 +724,10 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
     ks::set_reason(reason, len, "matmul: acc_stages must be 1 or 2 (TMEM accumulator buffers)");
     return KS_ERR_INVALID_CONFIG;
   }
-  if (cfg->group_m < 1 || cfg->group_m > 64) {
-    ks::set_reason(reason, len, "matmul: group_m must be 1..64");
+  if (cfg->group_m < -32 || cfg->group_m == 0 || cfg->group_m > 64) {
+    ks::set_reason(reason, len,
+                   "matmul: group_m must be 1..64 (raster groups of M-tiles) or -32..-1 (bands of N-tiles, B kept "
+                   "in L2)");
     return KS_ERR_INVALID_CONFIG;
   }
   const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages);

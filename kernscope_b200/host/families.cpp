@@ -239,9 +239,10 @@ class MatmulFamily : public Family {
     std::vector<json> v;
     // tile_m 128: one CTA per tile; tile_m 256: a CTA pair (cta_group::2)
     if (!full) {
+      // group_m: M-groups of 8 or 16 tiles, or bands of 8 N-tiles with B kept in L2
       for (auto [bn, st] : {std::pair{256, 3}, {256, 4}, {128, 4}, {128, 6}})
         for (int acc : {1, 2})
-          for (int g : {8, 16}) v.push_back(mm_json(128, bn, st, acc, g));
+          for (int g : {8, 16, -8}) v.push_back(mm_json(128, bn, st, acc, g));
       for (int st : {4, 6})
         for (int g : {8, 16}) v.push_back(mm_json(256, 256, st, 2, g));
       return v;
@@ -250,7 +251,7 @@ class MatmulFamily : public Family {
       for (int bn : {64, 128, 256})
         for (int st = 2; st <= 6; ++st)
           for (int acc : {1, 2})
-            for (int g : {1, 4, 8, 16, 32})
+            for (int g : {1, 4, 8, 16, 32, -8})
               if (bm == 128 || bn != 64) v.push_back(mm_json(bm, bn, st, acc, g));
     return v;
   }

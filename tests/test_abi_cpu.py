@@ -96,6 +96,8 @@ def test_kernel_symbols(N):
     assert N.kernel_symbol("softmax", N.SoftmaxConfig(256, 8, 0)) == "kernscope_b200_softmax_b256_v8_onepass"
     assert N.kernel_symbol("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 8)) == \
         "kernscope_b200_matmul_m128_n256_k64_s4_a2_g8"
+    assert N.kernel_symbol("matmul", N.MatmulConfig(128, 256, 64, 4, 2, -8)) == \
+        "kernscope_b200_matmul_m128_n256_k64_s4_a2_nb8"
     assert N.kernel_symbol("flash_attention", N.FlashAttentionConfig(128, 128, 2, 1)).endswith("_causal")
 
 

@@ -89,6 +89,24 @@ def test_matmul_ragged(ks, shape):
         assert_bf16_close(to_numpy(ops.matmul(a, b, cfg=cfg)), exp)
 
 
+@pytest.mark.parametrize("shape", [(1000, 2056, 264), (4096, 1024, 512), (130, 264, 72), (8192, 256, 128)])
+@pytest.mark.parametrize("tile_m", [128, 256])
+def test_matmul_nband_raster_bit_identical(ks, shape, tile_m):
+    """Negative group_m walks bands of N-tiles (N-tiles fastest, B loaded
+    evict_last).  The raster only reorders the tiles, so every band width
+    gives the bits of the M-group raster, including bands wider than the
+    N extent and ragged last bands."""
+    N, ops = ks
+    inp = oin.generate_inputs("matmul", shape, seed=5)
+    a, b = to_torch(inp["a"]), to_torch(inp["b"])
+    st = 4 if tile_m == 128 else 5
+    ref = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, st, 2, 8)))
+    assert_bf16_close(ref, orf.matmul(inp["a"], inp["b"]))
+    for g in (-1, -3, -8, -32):
+        got = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, st, 2, g)))
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), g
+
+
 @pytest.mark.parametrize("shape", [(5, 7, 9), (70, 33, 100), (64, 64, 13)])
 def test_matmul_unaligned_simt(ks, shape):
     _, ops = ks
@@ -138,3 +156,6 @@ def test_matmul_invalid_configs(ks):
     assert N.validate("matmul", N.MatmulConfig(128, 96, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(256, 64, 64, 4, 2, 8), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 6, 2, 8), 64, 64, 64)[0] == 0
+    for g in (0, -33, 65):
+        assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, g), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, -32), 64, 64, 64)[0] == 0

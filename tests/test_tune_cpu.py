@@ -31,12 +31,13 @@ def test_shape_hash_and_cache_key():
 
 def test_matmul_space():
     auto = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192])
-    assert len(auto) == 20 and all(v["valid"] for v in auto)
+    assert len(auto) == 28 and all(v["valid"] for v in auto)
     assert sum(v["config"]["tile_m"] == 256 for v in auto) == 4
+    assert sum(v["config"]["group_m"] < 0 for v in auto) == 8  # N-band rasters
     full = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192], full=True)
-    assert len(full) == 250
+    assert len(full) == 300
     bad = [v for v in full if not v["valid"]]
-    assert len(bad) == 20  # 5 and 6 stages of 128x256 tiles exceed 227 KB
+    assert len(bad) == 24  # 5 and 6 stages of 128x256 tiles exceed 227 KB
     assert all("stages" in v["reason"] for v in bad)
 
 
