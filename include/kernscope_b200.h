@@ -211,8 +211,8 @@ int ks_reduction_launch_noalloc(const ks_reduction_config *cfg, const ks_reducti
  * Config (sm_100a space): tile_m 128; tile_n {64,128,256}; tile_k 64;
  * stages 2..6 (2..4 at tile_n 256); acc_stages 1|2 (TMEM accumulator
  * buffers); group_m 1..64 (tile raster: M-tiles per L2 group) or -32..-1
- * (bands of -group_m N-tiles whose B panels are loaded evict_last, for
- * M >> N).  K % 8 == 0 and N % 8 == 0 (16-byte
+ * (bands of -group_m N-tiles whose B panels are loaded evict_last; tile_m
+ * 256 walks the same bands with plain loads).  K % 8 == 0 and N % 8 == 0 (16-byte
  * TMA strides); any M; pointers 16-byte aligned.                            */
 typedef struct ks_matmul_config {
   int tile_m; int tile_n; int tile_k; int stages; int acc_stages; int group_m;
