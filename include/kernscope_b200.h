@@ -208,14 +208,18 @@ int ks_reduction_launch_noalloc(const ks_reduction_config *cfg, const ks_reducti
  * C[M,N] = A[M,K] . B[K,N]; A row-major (K contiguous), B row-major
  * (N contiguous), C row-major; bf16 in/out, fp32 accumulate in TMEM.
  * Reference kernel arguments: (a, b, out, m, n, k).
- * Config (sm_100a space): tile_m 128; tile_n {64,128,256}; tile_k 64;
- * stages 2..6 (2..4 at tile_n 256); acc_stages 1|2 (TMEM accumulator
- * buffers); group_m 1..64 (tile raster: M-tiles per L2 group) or -32..-1
- * (bands of -group_m N-tiles whose B panels are loaded evict_last; tile_m
- * 256 walks the same bands with plain loads).  K % 8 == 0 and N % 8 == 0 (16-byte
+ * Config (sm_100a space): tile_m 128|256; tile_n {64,128,256} (128|256 at
+ * tile_m 256); tile_k 64; stages 2..6 (fewer where the ring would not fit
+ * 227 KB); acc_stages 1|2 (TMEM accumulator buffers, acc_stages x tile_n x
+ * tile_m/128 <= 512 columns for one-CTA tiles); group_m 1..64 (tile
+ * raster: M-tiles per L2 group) or -32..-1 (bands of -group_m N-tiles whose
+ * B panels are loaded evict_last; the CTA pair walks the same bands with
+ * plain loads); cta_group, for tile_m 256: 2 = a CTA pair issuing
+ * cta_group::2 M=256 MMAs across two SMs, 1 = one CTA issuing two M=128
+ * MMAs per B tile, 0 = the default (2).  K % 8 == 0 and N % 8 == 0 (16-byte
  * TMA strides); any M; pointers 16-byte aligned.                            */
 typedef struct ks_matmul_config {
-  int tile_m; int tile_n; int tile_k; int stages; int acc_stages; int group_m;
+  int tile_m; int tile_n; int tile_k; int stages; int acc_stages; int group_m; int cta_group;
 } ks_matmul_config;
 typedef struct ks_matmul_args {
   const void *a; const void *b; void *out; int64_t m; int64_t n; int64_t k;

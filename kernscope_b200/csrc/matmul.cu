@@ -3,7 +3,10 @@
 // The reference family (matmul_gen.cpp:287-402) stages fp32 copies of the
 // tiles in shared memory and accumulates with scalar FMAs.  Here:
 //
-//   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256),
+//   * persistent kernel, one CTA per SM, tiles of 128 x BN (BN 64/128/256)
+//     or, config tile_m 256 with cta_group 1, 256 x BN: two M=128 MMAs per
+//     K-step share each B tile, so a third less operand traffic reaches the
+//     SM per FLOP at BN 256 (TMEM: two accumulator halves of BN columns),
 //     raster grouped by `group_m` M-tiles for L2 reuse (or, group_m < 0,
 //     banded by N-tiles with the band's B panels kept in L2);
 //   * warp 0 (one lane) is the TMA producer: per K-block of 64 it loads the
@@ -41,11 +44,12 @@ constexpr uint32_t kBBoxBytes = kBK * 64 * 2;  // one B box: 64 K-rows x 64 N-co
 constexpr uint32_t kCBuf = 32 * 64;
 constexpr uint32_t kCStage = 4 * 2 * kCBuf;  // 4 warps x 2 buffers = 16 KB
 
-template <int BN, int STAGES, int ACC>
+template <int BN, int STAGES, int ACC, int MH = 1>
 struct MmLayout {
+  static constexpr uint32_t a_bytes = MH * kABytes;  // MH 128-row A boxes per stage
   static constexpr uint32_t b_bytes = kBK * BN * 2;
   static constexpr uint32_t a_off = 0;
-  static constexpr uint32_t b_off = a_off + STAGES * kABytes;
+  static constexpr uint32_t b_off = a_off + STAGES * a_bytes;
   static constexpr uint32_t c_off = b_off + STAGES * b_bytes;  // 1024-aligned (stage sizes are multiples of 8 KB)
   static constexpr uint32_t bar_off = c_off + kCStage;
   // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
@@ -53,9 +57,10 @@ struct MmLayout {
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t smem_request = bytes + 1024;  // slack to align the base to 1024
-  static constexpr uint32_t tmem_cols_raw = ACC * BN;
+  static constexpr uint32_t tmem_cols_raw = ACC * BN * MH;
   static constexpr uint32_t tmem_cols = tmem_cols_raw <= 32 ? 32 : tmem_cols_raw <= 64 ? 64
                                         : tmem_cols_raw <= 128 ? 128 : tmem_cols_raw <= 256 ? 256 : 512;
+  static_assert(tmem_cols_raw <= 512, "TMEM holds 512 columns");
 };
 
 // Output tile t of the persistent raster.  group_m > 0: groups of group_m
@@ -84,12 +89,13 @@ KS_DEV void tile_coords(int t, int num_m, int num_n, int group_m, int &tm, int &
   tn = r / gm;
 }
 
-template <int BN, int STAGES, int ACC>
+template <int BN, int STAGES, int ACC, int MH = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int group_m, int b3d,
                      KsWait wait) {
-  using L = MmLayout<BN, STAGES, ACC>;
+  using L = MmLayout<BN, STAGES, ACC, MH>;
+  constexpr int kTM = kBM * MH;  // output tile rows: MH M=128 MMAs share each B tile
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ks_smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -103,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_m = (M + kBM - 1) / kBM, num_n = (N + BN - 1) / BN;
+  const int num_m = (M + kTM - 1) / kTM, num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + kBK - 1) / kBK;
 
@@ -148,10 +154,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        uint8_t *a_dst = smem + L::a_off + stage * kABytes;
+        uint8_t *a_dst = smem + L::a_off + stage * L::a_bytes;
         uint8_t *b_dst = smem + L::b_off + stage * L::b_bytes;
-        ks_mbar_arrive_expect_tx(full + stage, kABytes + L::b_bytes);
-        ks_tma_load_2d(a_dst, &tma_a, full + stage, kb * kBK, tm * kBM);
+        ks_mbar_arrive_expect_tx(full + stage, L::a_bytes + L::b_bytes);
+#pragma unroll
+        for (int h = 0; h < MH; ++h) ks_tma_load_2d(a_dst + h * kABytes, &tma_a, full + stage, kb * kBK, tm * kTM + h * kBM);
         if (b3d) {
           // one copy for all BN/64 column blocks (tensor map dims: 64 columns, K, N/64)
           if (keep_b)
@@ -190,23 +197,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (i / ACC) & 1;
       if (!ks_mbar_wait(tempty + acc, acc_phase ^ 1u, abort, wait)) break;
       ks_tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BN;
+      const uint32_t d_tmem = tmem_base + acc * BN * MH;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait(full + stage, phase, abort, wait)) {
           ok = false;
           break;
         }
         ks_tc_fence_after();
-        const uint32_t a_addr = ks_smem_u32(smem + L::a_off + stage * kABytes);
+        const uint32_t a_addr = ks_smem_u32(smem + L::a_off + stage * L::a_bytes);
         const uint32_t b_addr = ks_smem_u32(smem + L::b_off + stage * L::b_bytes);
 #pragma unroll
         for (int k = 0; k < kBK / kUmmaK; ++k) {
-          // A: K-major, 128-byte rows, 8-row groups 1024 bytes apart; step 32 bytes per K=16.
-          const uint64_t adesc = ks_umma_desc_sw128(a_addr + k * 32, 16, 1024);
           // B: MN-major, 64-column boxes kBBoxBytes apart (LBO), 8 K-rows 1024 bytes apart (SBO);
           // step 16 K-rows = 2048 bytes per K=16.
           const uint64_t bdesc = ks_umma_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
-          ks_umma_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
+#pragma unroll
+          for (int h = 0; h < MH; ++h) {
+            // A: K-major, 128-byte rows, 8-row groups 1024 bytes apart; step 32 bytes per K=16.
+            const uint64_t adesc = ks_umma_desc_sw128(a_addr + h * kABytes + k * 32, 16, 1024);
+            ks_umma_ss(d_tmem + h * BN, adesc, bdesc, idesc, (kb | k) != 0);
+          }
         }
         ks_umma_commit(empty + stage);
         if (++stage == STAGES) {
@@ -237,13 +247,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       ks_tc_fence_after();
       int tm, tn;
       tile_coords(t, num_m, num_n, group_m, tm, tn);
-      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + acc * BN * MH;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < MH * (BN / 32); ++cc) {
+        const int h = cc / (BN / 32);  // 128-row half of the tile
         uint32_t r[32];
         ks_tmem_ld32(t_addr + cc * 32, r);
         ks_tmem_wait_ld();
-        if (cc + 1 == BN / 32) {  // the accumulator is free for the next tile's MMAs
+        if (cc + 1 == MH * (BN / 32)) {  // the accumulator is free for the next tile's MMAs
           ks_tc_fence_before();
           __syncwarp();
           if (lane == 0) ks_mbar_arrive(tempty + acc);
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ks_fence_proxy_async();  // the generic-proxy writes are visible to the TMA store
         __syncwarp();
         if (lane == 0) {
-          ks_tma_store_2d(&tma_c, buf, tn * BN + cc * 32, tm * kBM + q * 32);
+          ks_tma_store_2d(&tma_c, buf, tn * BN + (cc % (BN / 32)) * 32, tm * kTM + h * kBM + q * 32);
           ks_bulk_commit_group();
         }
         ++nstore;
@@ -568,9 +579,9 @@ bool tc_shape_ok(const ks_matmul_args &a) {
          a.n < (1LL << 31) && a.k < (1LL << 31);
 }
 
-template <int BN, int STAGES, int ACC>
+template <int BN, int STAGES, int ACC, int MH = 1>
 int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
-  using L = MmLayout<BN, STAGES, ACC>;
+  using L = MmLayout<BN, STAGES, ACC, MH>;
   CUtensorMap ta, tb;
   int s = ks::encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, uint64_t(a.k), uint64_t(a.m),
                              uint64_t(a.k) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -592,10 +603,10 @@ int launch_tc(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t
   s = ks::encode_tmap_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, uint64_t(a.n), uint64_t(a.m),
                          uint64_t(a.n) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (s != KS_OK) return s;
-  auto kern = matmul_tc_kernel<BN, STAGES, ACC>;
+  auto kern = matmul_tc_kernel<BN, STAGES, ACC, MH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::smem_request));
   if (e != cudaSuccess) return ks::map_cuda(e);
-  const int64_t tiles = ((a.m + kBM - 1) / kBM) * ((a.n + BN - 1) / BN);
+  const int64_t tiles = ((a.m + kBM * MH - 1) / (kBM * MH)) * ((a.n + BN - 1) / BN);
   const int sms = ks::sm_count();
   const int grid = int(tiles < sms ? tiles : sms);
   kern<<<grid, kThreads, L::smem_request, st>>>(ta, tb, tc, int(a.m), int(a.n), int(a.k), cfg.group_m, b3d,
@@ -682,14 +693,30 @@ int launch_tc_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaS
   }
 }
 
+// One CTA with 256-row tiles (two M=128 MMAs per B tile): the A ring holds
+// two 128-row boxes per stage.  tile_n 256: stages 2-3, one accumulator
+// (2 x 256 TMEM columns); tile_n 128: stages 2-4, one or two accumulators.
+template <int BN, int ACC>
+int launch_tc_wide_stages(const ks_matmul_config &cfg, const ks_matmul_args &a, cudaStream_t st) {
+  switch (cfg.stages) {
+    case 2: return launch_tc<BN, 2, ACC, 2>(cfg, a, st);
+    case 3: return launch_tc<BN, 3, ACC, 2>(cfg, a, st);
+    case 4: if constexpr (BN == 128) return launch_tc<BN, 4, ACC, 2>(cfg, a, st);
+      return KS_ERR_INVALID_CONFIG;
+    default: return KS_ERR_INVALID_CONFIG;
+  }
+}
+
 constexpr uint32_t kSmemLimit = 227 * 1024;
 
-// Per-CTA bytes: A ring + B ring (half of tile_n per CTA for the pair
-// kernel) + the C staging buffers of the TMA-store epilogue + barriers +
-// alignment slack.
-uint32_t smem_for(int bm, int bn, int stages) {
-  const uint32_t b_cols = bm == 256 ? uint32_t(bn / 2) : uint32_t(bn);
-  return uint32_t(stages) * (kABytes + uint32_t(kBK) * b_cols * 2) + kCStage + (2 * stages + 5) * 8 + 16 + 1024;
+// Per-CTA bytes: A ring (two 128-row boxes per stage for one-CTA 256-row
+// tiles) + B ring (half of tile_n per CTA for the pair kernel) + the C
+// staging buffers of the TMA-store epilogue + barriers + alignment slack.
+uint32_t smem_for(int bm, int bn, int stages, int cta_group) {
+  const bool pair = bm == 256 && cta_group != 1;
+  const uint32_t a_bytes = bm == 256 && !pair ? 2 * kABytes : kABytes;
+  const uint32_t b_cols = pair ? uint32_t(bn / 2) : uint32_t(bn);
+  return uint32_t(stages) * (a_bytes + uint32_t(kBK) * b_cols * 2) + kCStage + (2 * stages + 5) * 8 + 16 + 1024;
 }
 
 }  // namespace
@@ -700,22 +727,29 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
   if (!cfg) return KS_ERR_INVALID_ARGS;
   if (cfg->tile_m != 128 && cfg->tile_m != 256) {
     ks::set_reason(reason, len,
-                   "matmul: tile_m must be 128 (one CTA, UMMA M=128) or 256 (a CTA pair, cta_group::2 M=256)");
+                   "matmul: tile_m must be 128 (one CTA, UMMA M=128) or 256 (a CTA pair, cta_group::2 M=256, or one "
+                   "CTA with two M=128 MMAs)");
     return KS_ERR_INVALID_CONFIG;
   }
+  if (cfg->cta_group < 0 || cfg->cta_group > 2 || (cfg->tile_m == 128 && cfg->cta_group == 2)) {
+    ks::set_reason(reason, len, "matmul: cta_group must be 0 (default), 1, or 2 with tile_m 256");
+    return KS_ERR_INVALID_CONFIG;
+  }
+  const bool wide = cfg->tile_m == 256 && cfg->cta_group == 1;  // one CTA, 256-row tiles
   if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256) {
     ks::set_reason(reason, len, "matmul: tile_n must be 64, 128 or 256 (sm_100a space)");
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->tile_m == 256 && cfg->tile_n == 64) {
-    ks::set_reason(reason, len, "matmul: tile_m 256 needs tile_n 128 or 256 (each CTA loads tile_n/2 >= 64 columns)");
+    ks::set_reason(reason, len,
+                   "matmul: tile_m 256 needs tile_n 128 or 256 (a pair's CTA loads tile_n/2 >= 64 columns)");
     return KS_ERR_INVALID_CONFIG;
   }
   if (cfg->tile_k != 64) {
     ks::set_reason(reason, len, "matmul: tile_k must be 64 (one 128-byte swizzle row of bf16)");
     return KS_ERR_INVALID_CONFIG;
   }
-  const int max_st = (cfg->tile_n == 256 && cfg->tile_m == 128) ? 4 : 6;
+  const int max_st = wide ? (cfg->tile_n == 256 ? 3 : 4) : (cfg->tile_n == 256 && cfg->tile_m == 128) ? 4 : 6;
   if (cfg->stages < 2 || cfg->stages > max_st) {
     ks::set_reason(reason, len, "matmul: stages must be 2..%d for tile %dx%d", max_st, cfg->tile_m, cfg->tile_n);
     return KS_ERR_INVALID_CONFIG;
@@ -724,13 +758,18 @@ int ks_matmul_validate(const ks_matmul_config *cfg, int64_t m, int64_t n, int64_
     ks::set_reason(reason, len, "matmul: acc_stages must be 1 or 2 (TMEM accumulator buffers)");
     return KS_ERR_INVALID_CONFIG;
   }
+  if (wide && cfg->acc_stages * cfg->tile_n * 2 > 512) {
+    ks::set_reason(reason, len, "matmul: a one-CTA 256x%d tile with %d accumulators needs %d > 512 TMEM columns",
+                   cfg->tile_n, cfg->acc_stages, cfg->acc_stages * cfg->tile_n * 2);
+    return KS_ERR_INVALID_CONFIG;
+  }
   if (cfg->group_m < -32 || cfg->group_m == 0 || cfg->group_m > 64) {
     ks::set_reason(reason, len,
                    "matmul: group_m must be 1..64 (raster groups of M-tiles) or -32..-1 (bands of N-tiles, B kept "
                    "in L2)");
     return KS_ERR_INVALID_CONFIG;
   }
-  const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages);
+  const uint32_t smem = smem_for(cfg->tile_m, cfg->tile_n, cfg->stages, cfg->cta_group);
   if (smem > kSmemLimit) {
     ks::set_reason(reason, len, "matmul: %u bytes of shared memory for %d stages of %dx%dx64 > %u", smem,
                    cfg->stages, cfg->tile_m, cfg->tile_n, kSmemLimit);
@@ -763,6 +802,10 @@ int ks_matmul_launch(const ks_matmul_config *cfg, const ks_matmul_args *a, void 
     return ks::map_cuda(cudaGetLastError());
   }
   const bool two = cfg->acc_stages == 2;
+  if (cfg->tile_m == 256 && cfg->cta_group == 1) {  // one CTA, two M=128 MMAs per B tile
+    if (cfg->tile_n == 128) return two ? launch_tc_wide_stages<128, 2>(*cfg, *a, st) : launch_tc_wide_stages<128, 1>(*cfg, *a, st);
+    return launch_tc_wide_stages<256, 1>(*cfg, *a, st);
+  }
   if (cfg->tile_m == 256) {
     if (cfg->tile_n == 128) return two ? launch_tc2_stages<128, 2>(*cfg, *a, st) : launch_tc2_stages<128, 1>(*cfg, *a, st);
     return two ? launch_tc2_stages<256, 2>(*cfg, *a, st) : launch_tc2_stages<256, 1>(*cfg, *a, st);

@@ -25,9 +25,11 @@ extern "C" int ks_kernel_symbol(const char *family, const void *cfg, char *buf, 
   int n = -1;
   if (!strcmp(family, "matmul")) {
     auto c = static_cast<const ks_matmul_config *>(cfg);
-    // g<n>: raster groups of n M-tiles; nb<n>: bands of n N-tiles (group_m = -n)
-    n = snprintf(buf, len, "kernscope_b200_matmul_m%d_n%d_k%d_s%d_a%d_%s%d", c->tile_m, c->tile_n, c->tile_k,
-                 c->stages, c->acc_stages, c->group_m < 0 ? "nb" : "g", c->group_m < 0 ? -c->group_m : c->group_m);
+    // g<n>: raster groups of n M-tiles; nb<n>: bands of n N-tiles (group_m = -n);
+    // _c1: a 256-row tile on one CTA (the CTA pair is tile_m 256's default)
+    n = snprintf(buf, len, "kernscope_b200_matmul_m%d_n%d_k%d_s%d_a%d_%s%d%s", c->tile_m, c->tile_n, c->tile_k,
+                 c->stages, c->acc_stages, c->group_m < 0 ? "nb" : "g", c->group_m < 0 ? -c->group_m : c->group_m,
+                 c->tile_m == 256 && c->cta_group == 1 ? "_c1" : "");
   } else if (!strcmp(family, "flash_attention")) {
     auto c = static_cast<const ks_flash_attention_config *>(cfg);
     n = snprintf(buf, len, "kernscope_b200_flash_attention_br%d_bc%d_s%d%s", c->tile_m, c->tile_n, c->stages,

@@ -180,11 +180,18 @@ GateVerdict Session::verdict(const std::vector<float> &got, const std::vector<fl
 namespace {
 ks_matmul_config to_mm(const json &c) {
   return ks_matmul_config{iget(c, "tile_m", 128), iget(c, "tile_n", 256), iget(c, "tile_k", 64),
-                          iget(c, "stages", 4),   iget(c, "acc_stages", 2), iget(c, "group_m", 8)};
+                          iget(c, "stages", 4),   iget(c, "acc_stages", 2), iget(c, "group_m", 8),
+                          iget(c, "cta_group", 0)};
 }
-json mm_json(int bm, int bn, int st, int acc, int g) {
-  return db::json::object({{"tile_m", json(bm)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
-                           {"stages", json(st)}, {"acc_stages", json(acc)}, {"group_m", json(g)}});
+// cta_group appears only where it is not the tile_m default, so configs
+// recorded before it existed keep their keys
+json mm_json(int bm, int bn, int st, int acc, int g, int cg = 0) {
+  json j = db::json::object({{"tile_m", json(bm)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
+                             {"stages", json(st)}, {"acc_stages", json(acc)}, {"group_m", json(g)}});
+  if (cg == 1) j = db::json::object({{"tile_m", json(bm)}, {"tile_n", json(bn)}, {"tile_k", json(64)},
+                                      {"stages", json(st)}, {"acc_stages", json(acc)}, {"group_m", json(g)},
+                                      {"cta_group", json(cg)}});
+  return j;
 }
 int pow2_cols(int c) {
   int p = 32;
@@ -245,6 +252,12 @@ class MatmulFamily : public Family {
           for (int g : {8, 16, -8}) v.push_back(mm_json(128, bn, st, acc, g));
       for (int st : {4, 6})
         for (int g : {8, 16}) v.push_back(mm_json(256, 256, st, 2, g));
+      // 256-row tiles on one CTA (two M=128 MMAs per B tile)
+      for (int g : {16, -8}) {
+        v.push_back(mm_json(256, 256, 2, 1, g, 1));
+        v.push_back(mm_json(256, 256, 3, 1, g, 1));
+        v.push_back(mm_json(256, 128, 4, 2, g, 1));
+      }
       return v;
     }
     for (int bm : {128, 256})
@@ -253,26 +266,30 @@ class MatmulFamily : public Family {
           for (int acc : {1, 2})
             for (int g : {1, 4, 8, 16, 32, -8})
               if (bm == 128 || bn != 64) v.push_back(mm_json(bm, bn, st, acc, g));
+    for (int bn : {128, 256})
+      for (int st = 2; st <= 4; ++st)
+        for (int acc : {1, 2})
+          for (int g : {1, 4, 8, 16, 32, -8}) v.push_back(mm_json(256, bn, st, acc, g, 1));
     return v;
   }
   ConfigVerdict validate(const json &cfg, const std::vector<std::int64_t> &s, const std::string &arch) const override {
     MatmulConfig c{iget(cfg, "tile_m", 0), iget(cfg, "tile_n", 0), iget(cfg, "tile_k", 0), iget(cfg, "stages", 0),
-                   iget(cfg, "acc_stages", 0), iget(cfg, "group_m", 0)};
+                   iget(cfg, "acc_stages", 0), iget(cfg, "group_m", 0), iget(cfg, "cta_group", 0)};
     return validate_config(c, MatmulProblem{s[0], s[1], s[2], arch, 2});
   }
   Resources resources(const json &cfg, const std::vector<std::int64_t> &) const override {
     ks_matmul_config c = to_mm(cfg);
-    return Resources{64, int(smem_bytes(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m})),
-                     192, pow2_cols(c.acc_stages * c.tile_n)};
+    return Resources{64, int(smem_bytes(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m, c.cta_group})),
+                     192, pow2_cols(c.acc_stages * c.tile_n * (c.tile_m == 256 && c.cta_group == 1 ? 2 : 1))};
   }
   LaunchGeometry geometry(const json &cfg, const std::vector<std::int64_t> &s) const override {
     ks_matmul_config c = to_mm(cfg);
-    return launch_geometry(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m},
+    return launch_geometry(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m, c.cta_group},
                            MatmulProblem{s[0], s[1], s[2], "sm_100a", 2});
   }
   std::string symbol(const json &cfg) const override {
     ks_matmul_config c = to_mm(cfg);
-    return kernel_symbol(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m});
+    return kernel_symbol(MatmulConfig{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m, c.cta_group});
   }
   std::vector<std::int64_t> gate_shape(const std::vector<std::int64_t> &) const override { return {64, 64, 64}; }
   std::int64_t flops(const std::vector<std::int64_t> &s, const json &) const override {
@@ -300,7 +317,7 @@ class MatmulFamily : public Family {
       << "  void *a, *b, *c;\n  ks_gpu_malloc(&a, m * k * 2); ks_gpu_malloc(&b, k * n * 2); ks_gpu_malloc(&c, m * n * 2);\n"
       << "  ks_gpu_memset(a, 0, m * k * 2, nullptr); ks_gpu_memset(b, 0, k * n * 2, nullptr);\n"
       << "  ks_matmul_config cfg{" << c.tile_m << ", " << c.tile_n << ", " << c.tile_k << ", " << c.stages << ", "
-      << c.acc_stages << ", " << c.group_m << "};\n"
+      << c.acc_stages << ", " << c.group_m << ", " << c.cta_group << "};\n"
       << "  ks_matmul_args args{a, b, c, m, n, k};\n"
       << "  int st = ks_matmul_launch(&cfg, &args, nullptr);\n  if (st == 0) st = ks_gpu_synchronize();\n"
       << "  std::printf(\"%s\\n\", ks_status_string(st));\n  return st == 0 ? 0 : 1;\n}\n";
@@ -874,7 +891,7 @@ static ConfigVerdict check_arch(const std::string &arch) {
 
 ConfigVerdict validate_config(const MatmulConfig &c, const MatmulProblem &p) noexcept {
   if (auto a = check_arch(p.arch); !a.valid) return a;
-  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m};
+  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m, c.cta_group};
   char reason[256] = {0};
   ConfigVerdict v = from_status(ks_matmul_validate(&k, p.m, p.n, p.k, reason, sizeof(reason)), reason);
   if (!v.valid) return v;
@@ -882,7 +899,7 @@ ConfigVerdict validate_config(const MatmulConfig &c, const MatmulProblem &p) noe
   if (smem_bytes(c) > arch.smem_per_block_max_bytes)
     return {false, "matmul: shared memory " + std::to_string(smem_bytes(c)) + " > " +
                        std::to_string(arch.smem_per_block_max_bytes) + " bytes per CTA"};
-  if (pow2_cols(c.acc_stages * c.tile_n) > arch.tmem_columns_per_sm)
+  if (pow2_cols(c.acc_stages * c.tile_n * (c.tile_m == 256 && c.cta_group == 1 ? 2 : 1)) > arch.tmem_columns_per_sm)
     return {false, "matmul: accumulators need more than 512 TMEM columns"};
   return v;
 }
@@ -926,11 +943,14 @@ ConfigVerdict validate_config(const ReductionConfig &c, const ElemProblem &p) no
 }
 
 std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
-  // per CTA: A ring (128 x 64 bf16) + B ring (64 x tile_n bf16; half of tile_n
-  // for the CTA pair of tile_m 256) + the C staging of the TMA-store epilogue
-  // (4 warps x 2 x [32 x 32] bf16) + barriers + 1 KB alignment slack
-  const std::int64_t b_cols = c.tile_m == 256 ? c.tile_n / 2 : c.tile_n;
-  return std::int64_t(c.stages) * (128 * 64 * 2 + 64 * b_cols * 2) + 16384 +
+  // per CTA: A ring (128 x 64 bf16, two such boxes for a one-CTA 256-row
+  // tile) + B ring (64 x tile_n bf16; half of tile_n for the CTA pair of
+  // tile_m 256) + the C staging of the TMA-store epilogue (4 warps x 2 x
+  // [32 x 32] bf16) + barriers + 1 KB alignment slack
+  const bool pair = c.tile_m == 256 && c.cta_group != 1;
+  const std::int64_t a_rows = c.tile_m == 256 && !pair ? 256 : 128;
+  const std::int64_t b_cols = pair ? c.tile_n / 2 : c.tile_n;
+  return std::int64_t(c.stages) * (a_rows * 64 * 2 + 64 * b_cols * 2) + 16384 +
          (2 * c.stages + 2 * c.acc_stages + 1) * 8 + 16 + 1024;
 }
 
@@ -947,12 +967,13 @@ std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProbl
 LaunchGeometry launch_geometry(const MatmulConfig &c, const MatmulProblem &p) noexcept {
   LaunchGeometry g;
   const std::int64_t tiles = ((p.m + c.tile_m - 1) / c.tile_m) * ((p.n + c.tile_n - 1) / c.tile_n);
-  // persistent: one CTA per SM (tile_m 256: one CTA pair per two SMs)
+  // persistent: one CTA per SM (the CTA pair of tile_m 256: one pair per two SMs)
   const std::int64_t sms = device_sms();
-  g.grid_x = c.tile_m == 256 ? int(2 * std::min<std::int64_t>(tiles, sms / 2)) : int(std::min<std::int64_t>(tiles, sms));
+  const bool pair = c.tile_m == 256 && c.cta_group != 1;
+  g.grid_x = pair ? int(2 * std::min<std::int64_t>(tiles, sms / 2)) : int(std::min<std::int64_t>(tiles, sms));
   g.block_x = 192;
   g.smem_bytes = int(smem_bytes(c));
-  g.tmem_columns = pow2_cols(c.acc_stages * c.tile_n);
+  g.tmem_columns = pow2_cols(c.acc_stages * c.tile_n * (c.tile_m == 256 && !pair ? 2 : 1));
   return g;
 }
 
@@ -980,7 +1001,7 @@ static std::string sym(const char *fam, const void *cfg) {
   return ks_kernel_symbol(fam, cfg, buf, sizeof(buf)) == KS_OK ? std::string(buf) : std::string();
 }
 std::string kernel_symbol(const MatmulConfig &c) {
-  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m};
+  ks_matmul_config k{c.tile_m, c.tile_n, c.tile_k, c.stages, c.acc_stages, c.group_m, c.cta_group};
   return sym("matmul", &k);
 }
 std::string kernel_symbol(const FlashAttentionConfig &c) {

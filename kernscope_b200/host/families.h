@@ -41,6 +41,7 @@ struct LaunchGeometry {
 // --- typed configs (field names follow the C ABI structs) ------------------
 struct MatmulConfig {
   int tile_m = 128, tile_n = 256, tile_k = 64, stages = 4, acc_stages = 2, group_m = 8;
+  int cta_group = 0;  // tile_m 256: 2 (or 0) a CTA pair, 1 one CTA with two M=128 MMAs
 };
 struct MatmulProblem {
   std::int64_t m = 0, n = 0, k = 0;

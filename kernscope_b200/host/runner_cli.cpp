@@ -236,7 +236,8 @@ static int run_main(int argc, char **argv) {
   } else if (f == "matmul") {
     if (!need(2)) return usage("matmul takes two --in (a, b)");
     ks_matmul_config c{iget(cfg, "tile_m", 128), iget(cfg, "tile_n", 256), iget(cfg, "tile_k", 64),
-                       iget(cfg, "stages", 4), iget(cfg, "acc_stages", 2), iget(cfg, "group_m", 8)};
+                       iget(cfg, "stages", 4), iget(cfg, "acc_stages", 2), iget(cfg, "group_m", 8),
+                       iget(cfg, "cta_group", 0)};
     ks_matmul_args a{din[0].p, din[1].p, dout.p, i[0], i[1], i[2]};
     st = ks_matmul_launch(&c, &a, nullptr);
   } else {

@@ -76,7 +76,7 @@ class ReductionArgs(C.Structure):
 
 class MatmulConfig(C.Structure):
     _fields_ = [("tile_m", C.c_int), ("tile_n", C.c_int), ("tile_k", C.c_int), ("stages", C.c_int),
-                ("acc_stages", C.c_int), ("group_m", C.c_int)]
+                ("acc_stages", C.c_int), ("group_m", C.c_int), ("cta_group", C.c_int)]
 
 
 class MatmulArgs(C.Structure):

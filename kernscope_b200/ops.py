@@ -95,8 +95,9 @@ def default_reduction_config(cols: int, axis: int) -> N.ReductionConfig:
 
 def default_matmul_config(m: int, n: int, k: int) -> N.MatmulConfig:
     if n >= 256 and m * n >= 2048 * 2048:
+        # 256x256 tiles on one CTA (two M=128 MMAs per B tile, cta_group 1),
         # bands of 8 N-tiles whose B panels stay in L2 (group_m -8)
-        return N.MatmulConfig(128, 256, 64, 4, 2, -8)
+        return N.MatmulConfig(256, 256, 64, 3, 1, -8, 1)
     return N.MatmulConfig(128, 128, 64, 6, 2, 8)
 
 

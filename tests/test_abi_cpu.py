@@ -98,6 +98,10 @@ def test_kernel_symbols(N):
         "kernscope_b200_matmul_m128_n256_k64_s4_a2_g8"
     assert N.kernel_symbol("matmul", N.MatmulConfig(128, 256, 64, 4, 2, -8)) == \
         "kernscope_b200_matmul_m128_n256_k64_s4_a2_nb8"
+    assert N.kernel_symbol("matmul", N.MatmulConfig(256, 256, 64, 3, 1, -8, 1)) == \
+        "kernscope_b200_matmul_m256_n256_k64_s3_a1_nb8_c1"
+    assert N.kernel_symbol("matmul", N.MatmulConfig(256, 256, 64, 5, 2, 16)) == \
+        "kernscope_b200_matmul_m256_n256_k64_s5_a2_g16"  # the CTA pair keeps its name
     assert N.kernel_symbol("flash_attention", N.FlashAttentionConfig(128, 128, 2, 1)).endswith("_causal")
 
 

@@ -30,9 +30,12 @@ def ks(cuda_ok):
 
 
 def _configs(N):
-    """Every tile/stage/accumulator config: one CTA (tile_m 128) and CTA pairs (tile_m 256)."""
-    for bm, bn, st, acc in itertools.product((128, 256), (64, 128, 256), (2, 3, 4, 5, 6), (1, 2)):
-        cfg = N.MatmulConfig(bm, bn, 64, st, acc, 8)
+    """Every tile/stage/accumulator config: one CTA (tile_m 128), CTA pairs
+    (tile_m 256) and one-CTA 256-row tiles (tile_m 256, cta_group 1)."""
+    for bm, bn, st, acc, cg in itertools.product((128, 256), (64, 128, 256), (2, 3, 4, 5, 6), (1, 2), (0, 1)):
+        if cg == 1 and bm != 256:
+            continue
+        cfg = N.MatmulConfig(bm, bn, 64, st, acc, 8, cg)
         if N.validate("matmul", cfg, 64, 64, 64)[0] == 0:
             yield cfg
 
@@ -85,26 +88,32 @@ def test_matmul_ragged(ks, shape):
     exp = orf.matmul(inp["a"], inp["b"])
     a, b = to_torch(inp["a"]), to_torch(inp["b"])
     for cfg in (N.MatmulConfig(128, 256, 64, 4, 2, 8), N.MatmulConfig(128, 64, 64, 3, 1, 1),
-                N.MatmulConfig(256, 256, 64, 5, 2, 16), N.MatmulConfig(256, 128, 64, 3, 1, 1)):
+                N.MatmulConfig(256, 256, 64, 5, 2, 16), N.MatmulConfig(256, 128, 64, 3, 1, 1),
+                N.MatmulConfig(256, 256, 64, 3, 1, -8, 1), N.MatmulConfig(256, 128, 64, 4, 2, 3, 1)):
         assert_bf16_close(to_numpy(ops.matmul(a, b, cfg=cfg)), exp)
 
 
+# (tile_m, stages, acc_stages, cta_group): one CTA, CTA pair, one-CTA 256-row tile
+KINDS = [(128, 4, 2, 0), (256, 5, 2, 0), (256, 3, 1, 1)]
+
+
 @pytest.mark.parametrize("shape", [(1000, 2056, 264), (4096, 1024, 512), (130, 264, 72), (8192, 256, 128)])
-@pytest.mark.parametrize("tile_m", [128, 256])
-def test_matmul_nband_raster_bit_identical(ks, shape, tile_m):
+@pytest.mark.parametrize("kind", KINDS, ids=lambda t: f"m{t[0]}c{t[3]}")
+def test_matmul_nband_raster_bit_identical(ks, shape, kind):
     """Negative group_m walks bands of N-tiles (N-tiles fastest, B loaded
     evict_last).  The raster only reorders the tiles, so every band width
     gives the bits of the M-group raster, including bands wider than the
-    N extent and ragged last bands."""
+    N extent and ragged last bands; and every tile kind gives the bits of
+    the one-CTA 128-row kernel (each output accumulates K in order)."""
     N, ops = ks
+    tm, st, acc, cg = kind
     inp = oin.generate_inputs("matmul", shape, seed=5)
     a, b = to_torch(inp["a"]), to_torch(inp["b"])
-    st = 4 if tile_m == 128 else 5
-    ref = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, st, 2, 8)))
-    assert_bf16_close(ref, orf.matmul(inp["a"], inp["b"]))
-    for g in (-1, -3, -8, -32):
-        got = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, st, 2, g)))
-        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), g
+    base = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(128, 256, 64, 4, 2, 8)))
+    assert_bf16_close(base, orf.matmul(inp["a"], inp["b"]))
+    for g in (8, -1, -3, -8, -32):
+        got = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(tm, 256, 64, st, acc, g, cg)))
+        assert np.array_equal(got.view(np.uint16), base.view(np.uint16)), g
 
 
 @pytest.mark.parametrize("shape", [(5, 7, 9), (70, 33, 100), (64, 64, 13)])
@@ -129,12 +138,13 @@ def test_matmul_empty(ks):
     assert float(out.abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("tile_m", [128, 256])
-def test_matmul_8192_sampled(ks, tile_m):
+@pytest.mark.parametrize("kind", KINDS, ids=lambda t: f"m{t[0]}c{t[3]}")
+def test_matmul_8192_sampled(ks, kind):
     """C4 8192^3 with N(0, 1/sqrt(K)) operands: a full 128-row panel and 4096
     random elements against an fp32 reference (rel-err <= 1e-2)."""
     N, ops = ks
-    cfg = N.MatmulConfig(tile_m, 256, 64, 4 if tile_m == 128 else 5, 2, 16)
+    tm, st, acc, cg = kind
+    cfg = N.MatmulConfig(tm, 256, 64, st, acc, -8 if cg == 1 else 16, cg)
     m = n = k = 8192
     inp = oin.baseline_inputs("matmul", (m, n, k), seed=3)
     y = ops.matmul(to_torch(inp["a"]), to_torch(inp["b"]), cfg=cfg)
@@ -159,3 +169,11 @@ def test_matmul_invalid_configs(ks):
     for g in (0, -33, 65):
         assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, g), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
     assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, -32), 64, 64, 64)[0] == 0
+    # one-CTA 256-row tiles: three stages of 64 KB fit, four do not; two accumulators of 2 x 256 columns
+    # exceed TMEM; cta_group 2 needs tile_m 256; cta_group is 0, 1 or 2
+    assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 3, 1, 8, 1), 64, 64, 64)[0] == 0
+    assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 4, 1, 8, 1), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 3, 2, 8, 1), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(256, 128, 64, 4, 2, 8, 1), 64, 64, 64)[0] == 0
+    assert N.validate("matmul", N.MatmulConfig(128, 256, 64, 4, 2, 8, 2), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG
+    assert N.validate("matmul", N.MatmulConfig(256, 256, 64, 3, 1, 8, 3), 64, 64, 64)[0] == N.KS_ERR_INVALID_CONFIG

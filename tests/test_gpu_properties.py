@@ -33,17 +33,19 @@ def ks(cuda_ok):
     return native, ops, torch
 
 
-@pytest.mark.parametrize("tile_m", [128, 256])
+@pytest.mark.parametrize("kind", [(128, 4, 2, 16, 0), (256, 5, 2, 16, 0), (256, 3, 1, -8, 1)],
+                         ids=["m128", "pair", "m256c1"])
 @pytest.mark.parametrize("m", [8192, 65536])
-def test_matmul_permutation_gather_bit_exact(ks, m, tile_m):
+def test_matmul_permutation_gather_bit_exact(ks, m, kind):
     N, ops, torch = ks
+    tile_m, st, acc, grp, cg = kind
     n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(3)
     a = (torch.randn(m, k, generator=g, device="cuda") / 90.5).bfloat16()
     perm = torch.randperm(k, generator=g, device="cuda")
     b = torch.zeros(k, n, dtype=torch.bfloat16, device="cuda")
     b[perm, torch.arange(n, device="cuda")] = 1.0  # C[:, j] = A[:, perm[j]]
-    c = ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, 4 if tile_m == 128 else 5, 2, 16))
+    c = ops.matmul(a, b, cfg=N.MatmulConfig(tile_m, 256, 64, st, acc, grp, cg))
     torch.cuda.synchronize()
     assert torch.equal(c, a[:, perm])
     del a, b, c

@@ -31,14 +31,17 @@ def test_shape_hash_and_cache_key():
 
 def test_matmul_space():
     auto = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192])
-    assert len(auto) == 28 and all(v["valid"] for v in auto)
-    assert sum(v["config"]["tile_m"] == 256 for v in auto) == 4
-    assert sum(v["config"]["group_m"] < 0 for v in auto) == 8  # N-band rasters
+    assert len(auto) == 34 and all(v["valid"] for v in auto)
+    assert sum(v["config"]["tile_m"] == 256 for v in auto) == 10  # 4 CTA pairs, 6 one-CTA 256-row tiles
+    assert sum(v["config"].get("cta_group") == 1 for v in auto) == 6
+    assert sum(v["config"]["group_m"] < 0 for v in auto) == 11  # N-band rasters
     full = tune.query("enumerate", family="matmul", shape=[8192, 8192, 8192], full=True)
-    assert len(full) == 300
+    assert len(full) == 372
     bad = [v for v in full if not v["valid"]]
-    assert len(bad) == 24  # 5 and 6 stages of 128x256 tiles exceed 227 KB
-    assert all("stages" in v["reason"] for v in bad)
+    # 5 and 6 stages of 128x256 tiles, and 4 stages of one-CTA 256x256 tiles, exceed 227 KB; two
+    # accumulators of a one-CTA 256x256 tile exceed 512 TMEM columns
+    assert len(bad) == 48
+    assert all("stages" in v["reason"] or "TMEM" in v["reason"] for v in bad)
 
 
 def test_rowop_spaces_and_rejections():
@@ -148,7 +151,7 @@ def test_reproducer_source_mentions_config():
     g = tune.query("geometry", family="matmul", shape=[8192, 8192, 8192],
                    config={"tile_m": 128, "tile_n": 256, "tile_k": 64, "stages": 4, "acc_stages": 2, "group_m": 8})
     assert g["grid_x"] == 148 and g["block_x"] == 192 and g["tmem_columns"] == 512
-    assert "ks_matmul_launch" in g["source"] and "{128, 256, 64, 4, 2, 8}" in g["source"]
+    assert "ks_matmul_launch" in g["source"] and "{128, 256, 64, 4, 2, 8, 0}" in g["source"]
     assert g["gate_shape"] == [64, 64, 64]
 
 
