@@ -121,3 +121,46 @@ def test_strong_shards_partition_the_job(family):
             assert abs(sum(parts) - full) <= 1e-9 * full, (world, shards)
         if family.startswith("matmul"):
             assert all(sh[1:] == tuple(wl["shape"][1:]) for sh in shards)  # B replicated, K and N whole
+
+
+def _shard_status(N, ops, family, shape):
+    """(status, reason) of the family's validator for one shard, with the
+    config the benchmark launches for that shard (pointers are placeholders:
+    the validators read shapes and configs only)."""
+    p = 256
+    if family == "softmax":
+        return N.validate("softmax", ops.default_softmax_config(shape[1]), *shape)
+    if family == "layernorm":
+        return N.validate("layernorm", ops.default_layernorm_config(shape[1]), *shape)
+    if family in ("bias_gelu", "bias_gelu_erf"):
+        cfg = ops.default_bias_gelu_config(shape[1], "erf" if family == "bias_gelu_erf" else "tanh")
+        return N.validate("bias_gelu", cfg, shape[0] * shape[1], shape[1])
+    if family == "reduction":
+        a = N.ReductionArgs(p, p, shape[0], 1, N.KS_F32, N.KS_F32, -1, None, 0, None)
+        return N.validate("reduction", ops.default_reduction_config(shape[0], -1), a)
+    if family.startswith("matmul"):
+        return N.validate("matmul", ops.default_matmul_config(*shape), *shape)
+    b, h, s, d = shape
+    a = N.FlashAttentionArgs(p, p, p, p, b, h, s, s, d, d ** -0.5)
+    return N.validate("flash_attention", ops.default_flash_attention_config(True), a)
+
+
+@pytest.mark.parametrize("family", ["softmax", "layernorm", "bias_gelu", "bias_gelu_erf", "reduction", "matmul",
+                                    "matmul_65536", "flash_attention"])
+def test_strong_shards_pass_the_validators(family):
+    """Every rank's shard of a benchmark configuration at 1, 2, 4 and 8 GPUs
+    (the strong-scaling runs) is a shape the family's validator accepts with
+    the config the benchmark launches for it."""
+    import importlib.util
+
+    from kernscope_b200 import dist, native as N, ops
+
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    shape = bench.WORKLOADS[family]["shape"]
+    for world in (1, 2, 4, 8):
+        for r in range(world):
+            sh, _ = dist.strong_shard(family, shape, r, world)
+            st, why = _shard_status(N, ops, family, sh)
+            assert st == 0, (family, world, r, sh, why)
