@@ -96,6 +96,19 @@ KS_DEV void ks_mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
+// Non-blocking test of a phase (never suspends the thread).
+KS_DEV bool ks_mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 KS_DEV bool ks_mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -52,8 +52,8 @@ struct MmLayout {
   static constexpr uint32_t b_off = a_off + STAGES * a_bytes;
   static constexpr uint32_t c_off = b_off + STAGES * b_bytes;  // 1024-aligned (stage sizes are multiples of 8 KB)
   static constexpr uint32_t bar_off = c_off + kCStage;
-  // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC], drain
-  static constexpr uint32_t n_bars = 2 * STAGES + 2 * ACC + 1;
+  // full[STAGES], empty[STAGES], tfull[ACC], tempty[ACC * MH] (one per 128-row half), drain
+  static constexpr uint32_t n_bars = 2 * STAGES + ACC + ACC * MH + 1;
   static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t smem_request = bytes + 1024;  // slack to align the base to 1024
@@ -103,8 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *full = bars;
   uint64_t *empty = bars + STAGES;
   uint64_t *tfull = bars + 2 * STAGES;
-  uint64_t *tempty = bars + 2 * STAGES + ACC;
-  uint64_t *drain = bars + 2 * STAGES + 2 * ACC;
+  uint64_t *tempty = bars + 2 * STAGES + ACC;  // [acc * MH + half]
+  uint64_t *drain = bars + 2 * STAGES + ACC + ACC * MH;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::misc_off + 4);
 
@@ -118,10 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ks_mbar_init(full + s, 1);
       ks_mbar_init(empty + s, 1);
     }
-    for (int a = 0; a < ACC; ++a) {
-      ks_mbar_init(tfull + a, 1);
-      ks_mbar_init(tempty + a, 4);
-    }
+    for (int a = 0; a < ACC; ++a) ks_mbar_init(tfull + a, 1);
+    for (int a = 0; a < ACC * MH; ++a) ks_mbar_init(tempty + a, 4);
     ks_mbar_init(drain, 1);
     *abort = 0;
     ks_fence_mbar_init();
@@ -192,32 +190,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     int i = 0;
+    // MMAs of K-block kb for the 128-row halves [h0, h1) of the tile, from ring stage st
+    auto issue = [&](int st, int kb, uint32_t d_tmem, int h0, int h1) {
+      const uint32_t a_addr = ks_smem_u32(smem + L::a_off + st * L::a_bytes);
+      const uint32_t b_addr = ks_smem_u32(smem + L::b_off + st * L::b_bytes);
+#pragma unroll
+      for (int k = 0; k < kBK / kUmmaK; ++k) {
+        // B: MN-major, 64-column boxes kBBoxBytes apart (LBO), 8 K-rows 1024 bytes apart (SBO);
+        // step 16 K-rows = 2048 bytes per K=16.
+        const uint64_t bdesc = ks_umma_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
+#pragma unroll
+        for (int h = 0; h < MH; ++h) {
+          if (h < h0 || h >= h1) continue;
+          // A: K-major, 128-byte rows, 8-row groups 1024 bytes apart; step 32 bytes per K=16.
+          const uint64_t adesc = ks_umma_desc_sw128(a_addr + h * kABytes + k * 32, 16, 1024);
+          ks_umma_ss(d_tmem + h * BN, adesc, bdesc, idesc, (kb | k) != 0);
+        }
+      }
+    };
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
       const int acc = i % ACC;
       const uint32_t acc_phase = (i / ACC) & 1;
-      if (!ks_mbar_wait(tempty + acc, acc_phase ^ 1u, abort, wait)) break;
+      // The epilogue frees the accumulator one 128-row half at a time.  Half
+      // 0's MMAs start as soon as it is free; those of the other halves wait
+      // for theirs, deferred over at most STAGES - 1 K-blocks (their ring
+      // stages are released once they are issued), so the tensor core works
+      // on half 0 while the epilogue still drains the rest.
+      if (!ks_mbar_wait(tempty + acc * MH, acc_phase ^ 1u, abort, wait)) break;
       ks_tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN * MH;
+      bool rest_free = MH == 1;
+      int pend = 0;  // K-blocks before kb whose other-half MMAs are deferred
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!ks_mbar_wait(full + stage, phase, abort, wait)) {
           ok = false;
           break;
         }
         ks_tc_fence_after();
-        const uint32_t a_addr = ks_smem_u32(smem + L::a_off + stage * L::a_bytes);
-        const uint32_t b_addr = ks_smem_u32(smem + L::b_off + stage * L::b_bytes);
-#pragma unroll
-        for (int k = 0; k < kBK / kUmmaK; ++k) {
-          // B: MN-major, 64-column boxes kBBoxBytes apart (LBO), 8 K-rows 1024 bytes apart (SBO);
-          // step 16 K-rows = 2048 bytes per K=16.
-          const uint64_t bdesc = ks_umma_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
-#pragma unroll
-          for (int h = 0; h < MH; ++h) {
-            // A: K-major, 128-byte rows, 8-row groups 1024 bytes apart; step 32 bytes per K=16.
-            const uint64_t adesc = ks_umma_desc_sw128(a_addr + h * kABytes + k * 32, 16, 1024);
-            ks_umma_ss(d_tmem + h * BN, adesc, bdesc, idesc, (kb | k) != 0);
+        issue(stage, kb, d_tmem, 0, 1);
+        if (!rest_free) {
+          if (pend + 1 < STAGES && kb + 1 < num_kb &&
+              !ks_mbar_test_wait(ks_smem_u32(tempty + acc * MH + 1), acc_phase ^ 1u)) {
+            ++pend;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
+          for (int h = 1; h < MH && ok; ++h) ok = ks_mbar_wait(tempty + acc * MH + h, acc_phase ^ 1u, abort, wait);
+          if (!ok) break;
+          ks_tc_fence_after();
+          rest_free = true;
+          for (int p = pend; p > 0; --p) {
+            const int sp = (stage + STAGES - p) % STAGES;
+            issue(sp, kb - p, d_tmem, 1, MH);
+            ks_umma_commit(empty + sp);
+          }
+          pend = 0;
         }
+        issue(stage, kb, d_tmem, 1, MH);
         ks_umma_commit(empty + stage);
         if (++stage == STAGES) {
           stage = 0;
@@ -254,10 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         ks_tmem_ld32(t_addr + cc * 32, r);
         ks_tmem_wait_ld();
-        if (cc + 1 == MH * (BN / 32)) {  // the accumulator is free for the next tile's MMAs
+        if ((cc + 1) % (BN / 32) == 0) {  // this half is free for the next tile's MMAs
           ks_tc_fence_before();
           __syncwarp();
-          if (lane == 0) ks_mbar_arrive(tempty + acc);
+          if (lane == 0) ks_mbar_arrive(tempty + acc * MH + h);
         }
         if (num_kb == 0) continue;  // K = 0 is written by the host (zeros)
         uint8_t *buf = stg + (nstore & 1) * kCBuf;
@@ -716,7 +748,7 @@ uint32_t smem_for(int bm, int bn, int stages, int cta_group) {
   const bool pair = bm == 256 && cta_group != 1;
   const uint32_t a_bytes = bm == 256 && !pair ? 2 * kABytes : kABytes;
   const uint32_t b_cols = pair ? uint32_t(bn / 2) : uint32_t(bn);
-  return uint32_t(stages) * (a_bytes + uint32_t(kBK) * b_cols * 2) + kCStage + (2 * stages + 5) * 8 + 16 + 1024;
+  return uint32_t(stages) * (a_bytes + uint32_t(kBK) * b_cols * 2) + kCStage + (2 * stages + 7) * 8 + 16 + 1024;
 }
 
 }  // namespace

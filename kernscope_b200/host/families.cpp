@@ -950,8 +950,11 @@ std::int64_t smem_bytes(const MatmulConfig &c) noexcept {
   const bool pair = c.tile_m == 256 && c.cta_group != 1;
   const std::int64_t a_rows = c.tile_m == 256 && !pair ? 256 : 128;
   const std::int64_t b_cols = pair ? c.tile_n / 2 : c.tile_n;
+  // barriers: full/empty per stage, tile-full per accumulator, and
+  // tile-empty per accumulator (pair) or per accumulator and 128-row half
+  const std::int64_t halves = pair ? 1 : a_rows / 128;
   return std::int64_t(c.stages) * (a_rows * 64 * 2 + 64 * b_cols * 2) + 16384 +
-         (2 * c.stages + 2 * c.acc_stages + 1) * 8 + 16 + 1024;
+         (2 * c.stages + c.acc_stages + c.acc_stages * halves + 1) * 8 + 16 + 1024;
 }
 
 std::int64_t smem_bytes(const FlashAttentionConfig &c, const FlashAttentionProblem &p) noexcept {
