@@ -116,6 +116,32 @@ def test_matmul_nband_raster_bit_identical(ks, shape, kind):
         assert np.array_equal(got.view(np.uint16), base.view(np.uint16)), g
 
 
+@pytest.mark.parametrize("shape", [(4096, 4096, 64), (4096, 4096, 192), (4096, 4096, 1024)])
+def test_matmul_wide_tiles_many_per_cta_bit_identical(ks, shape):
+    """One-CTA 256-row tiles free their accumulator one 128-row half at a
+    time, and the next tile's MMAs for the other half wait for it over up to
+    stages - 1 K-blocks.  With more tiles than SMs each CTA crosses several
+    tile boundaries; K of 1, 3 and 16 K-blocks covers the cases with no
+    deferral, with a deferral cut short by the last K-block, and with the
+    full one.  Every valid configuration gives the bits of the 128-row
+    kernel (each output accumulates K in order)."""
+    N, ops = ks
+    m, n, k = shape
+    inp = oin.generate_inputs("matmul", shape, seed=6)
+    a, b = to_torch(inp["a"]), to_torch(inp["b"])
+    base = to_numpy(ops.matmul(a, b, cfg=N.MatmulConfig(128, 256, 64, 4, 2, 8)))
+    n_cfg = 0
+    for bn, st, acc in itertools.product((64, 128, 256), (2, 3, 4, 5, 6), (1, 2)):
+        cfg = N.MatmulConfig(256, bn, 64, st, acc, -8, 1)
+        if N.validate("matmul", cfg, m, n, k)[0] != 0:
+            continue
+        assert (m // 256) * (n // bn) > 148  # several tiles per CTA
+        got = to_numpy(ops.matmul(a, b, cfg=cfg))
+        assert np.array_equal(got.view(np.uint16), base.view(np.uint16)), (bn, st, acc)
+        n_cfg += 1
+    assert n_cfg >= 6
+
+
 @pytest.mark.parametrize("shape", [(5, 7, 9), (70, 33, 100), (64, 64, 13)])
 def test_matmul_unaligned_simt(ks, shape):
     _, ops = ks
