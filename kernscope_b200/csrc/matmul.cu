@@ -19,8 +19,11 @@
 //     tcgen05.commit releases each ring slot and, per tile, signals the
 //     epilogue; warp 1 also owns the TMEM allocation;
 //   * warps 2-5 are the epilogue: each reads its 32-lane quadrant of the
-//     fp32 accumulator with tcgen05.ld, rounds to bf16 once and stores 16-byte
-//     vectors; ACC TMEM buffers let the next tile's MMAs run meanwhile.
+//     fp32 accumulator with tcgen05.ld, rounds to bf16 once and stores the
+//     tile with TMA through swizzled shared-memory staging; ACC TMEM buffers
+//     let the next tile's MMAs run meanwhile, and with 256-row tiles each
+//     128-row half is freed as soon as it is drained, so the next tile's
+//     half-0 MMAs overlap the drain of half 1.
 //
 // Every mbarrier wait is bounded (KsWait): on timeout the kernel records the
 // error word, waits (bounded) for its own TMA loads and MMAs, frees TMEM and
